@@ -1,0 +1,355 @@
+"""Benchmark of the B200 Qwen3 F32 decode path (BASELINE.json metric).
+
+Workload: Qwen3-0.6B architecture, F32, batch 1, random
+N(0, 0.02) weights from a seeded GGUF (norm weights 1.0), a 32-token prompt of
+seeded uniform ids, greedy decode. One "step" is one decode token: a full
+forward pass of the 28 layers + LM head + greedy sampling at the next position.
+The timed K steps continue the 32-token prompt (positions 32..32+K-1), exactly
+the reference benchmark's pg phase (benchmarks/cuda/bench.cpp Runner::evaluate).
+
+value: decode tokens/s with everything resident in HBM (CUDA-graph replay, token
+fed back on the device), timed with CUDA events on the engine's stream.
+e2e:   the same metric through the public C ABI call b200_engine_eval with host
+buffers: every step copies the input id host->device and reads the sampled id
+device->host (4 B each way).
+Inputs are larger than L2: every step streams 2.38 GB of weights (L2 is 126 MB).
+
+Multi-GPU (torchrun, --gpus N): the 0.6B model does not shard; every rank runs an
+independent replica (weak scaling) and value is the sum of the ranks' tokens over
+the slowest rank's time. --model 8b instead runs Qwen3-8B tensor-parallel over the
+N ranks (one NCCL all-reduce after o_proj and after ffn_down).
+
+--impl reference times the reference's own CPU implementation (the Infer-LLM CPU
+backend built from source into oracle/_ref) on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(REPO, "infer-llm_b200"), os.path.join(REPO, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+PROMPT_LEN = 32
+SEED = 0
+METRIC = "decode tok/s (Qwen3-0.6B-shape F32 bs1, 32-token prompt, greedy)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def model_cfg(name):
+    from b200infer import gguf as G
+    return {"0.6b": G.QWEN3_0_6B, "8b": G.QWEN3_8B}[name]
+
+
+def prompt_ids(cfg):
+    return np.random.default_rng(SEED).integers(0, cfg.n_vocab, PROMPT_LEN).astype(np.int32)
+
+
+def step_bytes(cfg, ctx_len: int) -> int:
+    """Algorithmic HBM bytes of one decode token: weights + KV read at ctx_len + KV write."""
+    kv_row = cfg.n_layer * 2 * cfg.n_head_kv * cfg.head_dim * 4
+    return cfg.weight_bytes_per_token + 4 * cfg.n_embd + kv_row * ctx_len + kv_row
+
+
+def gemv_bytes(cfg):
+    """Weight bytes each decode GEMV class streams per token (all layers)."""
+    H, D, F, L = cfg.n_embd, cfg.head_dim, cfg.n_ff, cfg.n_layer
+    return {"qkv_gemv": L * 4 * (cfg.n_head + 2 * cfg.n_head_kv) * D * H,
+            "o_proj_gemv": L * 4 * H * cfg.n_head * D,
+            "gate_up_gemv": L * 4 * 2 * F * H,
+            "down_gemv": L * 4 * H * F,
+            "lm_head_gemv": 4 * cfg.n_vocab * H}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import b200infer as B
+    from b200infer import gguf as G
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    cfg = model_cfg(args.model)
+    tp = args.model == "8b" and world > 1
+    steps, warm = args.steps, args.warmup
+    cap = PROMPT_LEN + max(steps, 128) + warm + 8
+    eng = B.Engine(cfg, kv_capacity=cap, max_batch=PROMPT_LEN, device=local,
+                   tp_rank=rank if tp else 0, tp_world=world if tp else 1)
+    if args.model == "0.6b":
+        path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", f"/tmp/b200_models_{local}"))
+        eng.load_gguf(path)
+    else:
+        eng.init_random(SEED)
+    if tp:
+        uid = [B.Engine.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.tp_init(uid[0])
+    eng.finalize()
+    prompt = prompt_ids(cfg)
+    stream = torch.cuda.ExternalStream(eng.stream())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- warm-up: prefill + W decode steps (also builds the CUDA graph)
+    eng.reset()
+    eng.eval(prompt)
+    eng.generate(warm)
+    # ---- TTFT: prefill of the 32-token prompt + first greedy token (host ids in, token out)
+    ttft = []
+    for _ in range(3):
+        eng.reset()
+        barrier()
+        t0 = time.perf_counter()
+        first = eng.eval(prompt)
+        ttft.append((time.perf_counter() - t0) * 1e3)
+    # ---- value: K decode steps, device resident, CUDA events on the engine stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        toks = eng.generate(steps)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    units = steps * (1 if tp else world)  # TP: one stream of tokens; replicas: one per rank
+    value = units / (ms_max / 1e3)
+    # ---- e2e through the public call with host buffers (H2D id, D2H token per step)
+    eng.reset()
+    tok = eng.eval(prompt)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    host_tok = np.array([tok], np.int32)
+    for _ in range(steps):
+        tok = eng.eval(host_tok)
+        host_tok[0] = tok
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = units / (e2e_ms / 1e3)
+    # ---- per-op breakdown of one eager decode step (events after each launch)
+    ops = {}
+    if not tp:
+        import ctypes as C
+        names = C.create_string_buffer(32 * 32)
+        us = (C.c_float * 32)()
+        reps = 5
+        for _ in range(reps):
+            n = B.lib().b200_engine_profile_step(eng.h, names, 32, us, 32)
+            if n < 0:
+                break
+            for i in range(n):
+                nm = names.raw[i * 32:(i + 1) * 32].split(b"\0")[0].decode()
+                ops[nm] = ops.get(nm, 0.0) + us[i] / reps
+    hbm, peak_kind = peaks()
+    ctx_mid = PROMPT_LEN + steps // 2
+    res = {
+        "metric": METRIC if args.model == "0.6b" else METRIC.replace("0.6B", "8B") + f" TP{world}",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"Qwen3-{'0.6B' if args.model == '0.6b' else '8B'} F32 decode, bs1, prompt "
+                               f"{PROMPT_LEN}, positions {PROMPT_LEN}..{PROMPT_LEN + steps - 1}",
+                   "weights": f"seeded N(0,0.02) ({'GGUF' if args.model == '0.6b' else 'on-device Philox'}, seed {SEED})",
+                   "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
+                   "l2": "inputs larger than L2 (2.38 GB of weights streamed per step)"},
+        "ttft_ms": round(float(np.median(ttft)), 3),
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": steps * (6 * cfg.n_layer + 1) if not tp else None,
+        "clocks": clk.summary(),
+    }
+    if ops:
+        gb = gemv_bytes(cfg)
+        gemv_us = sum(ops.get(k, 0.0) for k in gb)
+        gemv_total = sum(gb.values())
+        achieved = gemv_total / (gemv_us * 1e-6) / 1e9 if gemv_us else 0.0
+        res["roofline"] = {"bound": "hbm", "kernel": "gemv_kernel (all decode GEMVs of one token)",
+                           "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                           "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": None}
+        step_gbs = step_bytes(cfg, ctx_mid) / (ms_max / steps * 1e-3) / 1e9
+        res["step_roofline"] = {"achieved": round(step_gbs, 1), "frac": round(step_gbs / hbm, 4),
+                                "bytes_per_step": step_bytes(cfg, ctx_mid)}
+        res["ops_us_per_step_eager"] = {k: round(v, 2) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
+    if rank == 0 and world == 1 and args.model == "0.6b" and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_threads, sample_steps=args.cpu_sample_steps)
+    res["first_tokens"] = [int(first)] + [int(t) for t in toks[:8]]
+    if tp:
+        eng.close()
+        dist.destroy_process_group()
+    elif world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def cpu_baseline(cfg, threads=0, sample_steps=16):
+    """The reference CPU engine on a bounded sample: prefill 32 + `sample_steps` decode tokens."""
+    import oracle
+    from b200infer import gguf as G
+    threads = threads or (os.cpu_count() or 1)
+    if not oracle.Ref.available():
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+    ref = oracle.Ref()
+    path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", "/tmp/b200_models_0"))
+    eng = oracle.RefEngine(ref, path, threads=threads, capacity=PROMPT_LEN + sample_steps + 1)
+    t0 = time.perf_counter()
+    tok = eng.eval(prompt_ids(cfg))
+    t1 = time.perf_counter()
+    for _ in range(sample_steps):
+        tok = eng.eval(np.array([tok], np.int32))
+    t2 = time.perf_counter()
+    eng.close()
+    return {"value": round(sample_steps / (t2 - t1), 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "ttft_ms": round((t1 - t0) * 1e3, 1),
+            "sample": f"reference CPU backend, prompt {PROMPT_LEN} then {sample_steps} greedy decode tokens "
+                      f"(INFERLLM_THREADS={threads})"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle
+    from b200infer import gguf as G
+    cfg = model_cfg(args.model)
+    if args.model != "0.6b":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference CPU path at the 8B shape is only "
+                          "timed for the 0.6B workload"}))
+        return
+    if not oracle.Ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference built from source) missing"}))
+        return
+    threads = args.cpu_threads or (os.cpu_count() or 1)
+    ref = oracle.Ref()
+    path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", "/tmp/b200_models_0"))
+    steps, warm = args.steps, args.warmup
+    eng = oracle.RefEngine(ref, path, threads=threads, capacity=PROMPT_LEN + steps + warm + 8)
+    tok = eng.eval(prompt_ids(cfg))
+    for _ in range(warm):
+        tok = eng.eval(np.array([tok], np.int32))
+    eng.reset()
+    t0 = time.perf_counter()
+    tok = eng.eval(prompt_ids(cfg))
+    ttft = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    for _ in range(steps):
+        tok = eng.eval(np.array([tok], np.int32))
+    dt = time.perf_counter() - t1
+    eng.close()
+    value = steps / dt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"Qwen3-0.6B F32 decode, bs1, prompt {PROMPT_LEN}, positions "
+                               f"{PROMPT_LEN}..{PROMPT_LEN + steps - 1}", "weights": f"seeded GGUF seed {SEED}",
+                   "parallelism": "single"},
+        "ttft_ms": round(ttft * 1e3, 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{steps} greedy decode tokens after a {PROMPT_LEN}-token prefill"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--model", choices=["0.6b", "8b"], default="0.6b")
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--cpu-sample-steps", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,221 @@
+/*
+ * b200_infer.h -- C ABI of the B200-native (sm_100a) kernels and runtime for the
+ * Infer-LLM F32 Qwen3 inference path.
+ *
+ * The reference's kernel seam is
+ *     namespace CUDA_F32 { cudaError_t compute_<op>(Tensor* dst, cudaStream_t); }
+ * (include/kernels/cuda/kernel_f32.hpp:8-28), which hands the whole C++ Tensor
+ * struct across the call. This header replaces it with plain pointers, int64
+ * sizes and explicit strides, so any host language can bind it (ctypes, cgo,
+ * JNI). Conventions shared by every entry point:
+ *
+ *   - Layouts follow the reference's ggml convention (dims[0] fastest): a
+ *     weight "[K, N]" is N rows of K contiguous floats; activations "[K, M]"
+ *     are M rows (tokens) of K floats.
+ *   - All tensor pointers are device pointers on the current CUDA device unless
+ *     the name says host_. `stream` is a cudaStream_t (NULL = legacy stream).
+ *   - Entry points validate sizes on the host, enqueue work and return; they
+ *     never allocate, never synchronize and never trap. Scratch memory comes
+ *     from a caller-provided workspace whose size a *_workspace_bytes() query
+ *     returns.
+ *   - Device-side checks (token ids, positions) never fault: an offending row
+ *     is skipped and the first error is recorded in an optional device status
+ *     word (int32, 0 = ok) that the caller reads after the step.
+ *   - Return value: B200_OK or a B200_ERR_* code. The reference maps CUDA
+ *     failures to std::errc::io_error (include/cuda_util.hpp:7-16) and an
+ *     unknown op to std::errc::not_supported (src/backends/cuda_backend.cpp:237).
+ */
+#ifndef B200_INFER_H
+#define B200_INFER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT 1 /* std::errc::invalid_argument */
+#define B200_ERR_NOT_SUPPORTED 2    /* std::errc::not_supported */
+#define B200_ERR_OUT_OF_RANGE 3     /* bad token id / position / KV capacity */
+#define B200_ERR_CUDA 4             /* std::errc::io_error in the reference */
+#define B200_ERR_NO_MEMORY 5        /* std::errc::not_enough_memory */
+#define B200_ERR_DEVICE_CHECK 6     /* a device-side check set the status word */
+#define B200_ERR_TIMEOUT 7          /* a bounded device wait gave up */
+#define B200_ERR_NUMERIC 8          /* NaN / +inf logits (sampler.cpp:53) */
+
+/* Device status word codes (written by kernels, read by the host). */
+#define B200_DEV_BAD_TOKEN 1
+#define B200_DEV_BAD_POSITION 2
+#define B200_DEV_BAD_LOGITS 3
+#define B200_DEV_TIMEOUT 4
+
+/* Precision of a matrix product. */
+#define B200_PREC_FFMA 0 /* exact F32 FFMA (reference tolerance 1e-5) */
+#define B200_PREC_TF32 1 /* tcgen05 tensor cores, TF32 inputs, F32 accumulate */
+
+const char *b200_status_string(int status);
+/* 1 if the library was built for and runs on an sm_100 device, else 0. */
+int b200_device_supported(int device);
+
+/* ------------------------------------------------------------------------
+ * Single ops: one entry point per reference CUDA_F32::compute_* function.
+ * ------------------------------------------------------------------------ */
+
+/* out[t*N + n] = sum_k x[t*K + k] * w[n*K + k]   (y = x . W^T)
+ * Replaces CUDA_F32::compute_mul_mat (kernel_f32.hpp:18, kernel_f32.cu:180-205).
+ * M <= 4 uses the HBM-streaming GEMV (TMA bulk-staged weight tiles); larger M
+ * uses the tiled GEMM selected by `precision`. */
+int b200_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
+                 int precision, void *stream);
+
+/* Row-wise RMSNorm over D contiguous floats: y = x * rsqrt(mean(x^2) + eps) * gamma.
+ * Replaces CUDA_F32::compute_rms_norm (kernel_f32.hpp:14, kernel_f32.cu:60-90). */
+int b200_rms_norm(const float *x, const float *gamma, float *out, int64_t D, int64_t rows,
+                  float eps, void *stream);
+
+/* NeoX half-split RoPE of x [D, H, T] (x may equal out). Angles come from the
+ * reference's table layout [n_ctx][D/2] (theta_table, device memory), row pos[t].
+ * A position outside [0, n_ctx) leaves its rows untouched and records
+ * B200_DEV_BAD_POSITION (the reference kernel traps instead, kernel_f32.cu:250-253).
+ * Replaces CUDA_F32::compute_rope (kernel_f32.hpp:22, kernel_f32.cu:273-301). */
+int b200_rope(const float *x, const int32_t *pos, const float *theta_table, int64_t n_ctx,
+              float *out, int64_t D, int64_t H, int64_t T, int32_t *dev_status, void *stream);
+
+/* Fused per-head RMSNorm + RoPE (+ optional KV-cache write) for Q and K of one step.
+ * q_in [Dq*Hq] and k_in [D*Hkv] per token (row strides q_ld / k_ld floats), gammas
+ * [D]. Angles are float(double(pos) * freq[j]) with freq[j] = 1.0f/powf(theta, 2j/D),
+ * which reproduces the reference table (graph.cpp:119-131) bit for bit. q_out gets
+ * [D, Hq, T]; k_out (may be a KV-cache slot) gets [D, Hkv, T] with token stride
+ * k_out_ld floats. v_in/v_out optionally copy V into its cache slot in the same pass.
+ * Chains reference nodes rms_norm(q), rms_norm(k), rope(q), rope(k), cpy(k), cpy(v)
+ * (Qwen3.cpp:66-84). */
+int b200_qk_norm_rope(const float *q_in, int64_t q_ld, const float *k_in, int64_t k_ld,
+                      const float *v_in, int64_t v_ld, const float *q_gamma,
+                      const float *k_gamma, const float *freq, const int32_t *pos,
+                      float *q_out, float *k_out, int64_t k_out_ld, float *v_out,
+                      int64_t v_out_ld, int64_t D, int64_t Hq, int64_t Hkv, int64_t T,
+                      int64_t n_ctx, float eps, int32_t *dev_status, void *stream);
+
+/* Host helper: freq[j] = 1.0f / powf(theta, 2.0f*j/D), j < D/2 (host memory). */
+void b200_rope_freqs(float theta, int64_t D, float *host_freq);
+
+/* Causal GQA attention over a KV cache.
+ * q [D, Hq, Tq] contiguous; K/V element (token t, kv head h, dim d) at
+ * k[t*k_tok_stride + h*k_head_stride + d] (the reference cache is token-major:
+ * k_tok_stride = Hkv*D, k_head_stride = D); out [D, Hq, Tq].
+ * Key j is visible to query i iff j <= n_past + i; Tkv = n_past + Tq.
+ * scale <= 0 selects 1/sqrt(D). Decode (Tq small) uses split-KV flash-decoding
+ * with an in-kernel merge; prefill uses a tiled online-softmax kernel. Scratch for
+ * the split-KV partials comes from `workspace` (b200_flash_attn_workspace_bytes).
+ * Replaces CUDA_F32::compute_flash_attn (kernel_f32.hpp:24, kernel_f32.cu:452-511),
+ * which mallocs an Hq*Tq*Tkv score matrix and synchronizes on every call. */
+int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D,
+                    int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past,
+                    float scale, int64_t k_tok_stride, int64_t k_head_stride,
+                    int64_t v_tok_stride, int64_t v_head_stride, void *workspace,
+                    size_t workspace_bytes, void *stream);
+size_t b200_flash_attn_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64_t Tq,
+                                       int64_t Tkv);
+
+/* Elementwise ops of the reference graph (n elements).
+ * CUDA_F32::compute_silu / compute_mul / compute_add (kernel_f32.cu:529-630). */
+int b200_silu(const float *x, float *out, int64_t n, void *stream);
+int b200_mul(const float *a, const float *b, float *out, int64_t n, void *stream);
+int b200_add(const float *a, const float *b, float *out, int64_t n, void *stream);
+/* out = up * silu(gate): silu + mul of Qwen3.cpp:109-112 in one pass. */
+int b200_swiglu(const float *gate, const float *up, float *out, int64_t n, void *stream);
+
+/* Embedding gather out[t] = table[ids[t]] (rows of D floats, n_rows rows).
+ * An id outside [0, n_rows) leaves its row untouched and records B200_DEV_BAD_TOKEN.
+ * Replaces CUDA_F32::compute_get_rows (kernel_f32.hpp:16, kernel_f32.cu:107-138). */
+int b200_get_rows(const float *table, const int32_t *ids, float *out, int64_t D, int64_t n,
+                  int64_t n_rows, int32_t *dev_status, void *stream);
+
+/* Device-to-device copy of `bytes` (the reference's CPY / RESHAPE nodes,
+ * kernel_f32.cu:210-240, 305-319). */
+int b200_copy(void *dst, const void *src, size_t bytes, void *stream);
+
+/* Greedy sampler on the device: out_id = first index of the maximum of logits[n];
+ * NaN or +inf -> out_id = -1 and B200_DEV_BAD_LOGITS (sampler.cpp:42-65).
+ * workspace: b200_argmax_workspace_bytes(n). */
+int b200_argmax(const float *logits, int64_t n, int32_t *out_id, void *workspace,
+                size_t workspace_bytes, int32_t *dev_status, void *stream);
+size_t b200_argmax_workspace_bytes(int64_t n);
+
+/* ------------------------------------------------------------------------
+ * Qwen3 engine: device-resident weights, KV cache and activation arenas, the
+ * fused per-layer kernel sequence, CUDA-graph decode. It is the runtime behind
+ * the reference's Backend::compute for a Qwen3 graph (Qwen3.cpp:4-136,
+ * scheduler.cpp:4-28) without per-step graph building or allocation.
+ * ------------------------------------------------------------------------ */
+typedef struct b200_qwen3_config {
+    int32_t n_vocab, n_embd, n_layer, n_head, n_head_kv, head_dim, n_ff;
+    int32_t n_ctx_train;
+    float rope_theta, rms_eps;
+    int32_t tied;          /* LM head = token_embd (model.cpp:203-206) */
+    int32_t kv_capacity;   /* max tokens per sequence (KVCacheConfig) */
+    int32_t max_batch;     /* max tokens per eval call (prefill chunk) */
+    int32_t precision;     /* B200_PREC_* for prefill matrix products */
+    /* tensor parallelism (1 = single GPU); rank/world index this process */
+    int32_t tp_rank, tp_world;
+} b200_qwen3_config;
+
+typedef struct b200_engine b200_engine;
+
+/* Creates an engine on `device` and allocates its arenas once (weights, KV,
+ * activations, workspaces). Returns B200_ERR_NO_MEMORY if they do not fit. */
+int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **out);
+void b200_engine_destroy(b200_engine *e);
+/* Bytes the engine allocated, by arena (weights, kv, activations). */
+int b200_engine_memory(const b200_engine *e, size_t *weights, size_t *kv, size_t *act);
+
+/* Uploads one GGUF tensor (F32, host memory, numpy-style row-major (N, K)) by its
+ * GGUF name, e.g. "blk.3.attn_q.weight". Under tensor parallelism the engine keeps
+ * only its rank's shard of the full tensor passed here. */
+int b200_engine_set_weight(b200_engine *e, const char *name, const float *host_data,
+                           int64_t n_elements);
+/* Fills every weight from the seeded generator of the given seed directly on the
+ * device: matrices N(0, std), norm weights 1.0 (used when no GGUF is at hand). */
+int b200_engine_init_random(b200_engine *e, uint64_t seed, float std);
+/* Checks that every weight is set and prepares the decode CUDA graph. */
+int b200_engine_finalize(b200_engine *e);
+
+/* Drops the sequence (n_past = 0). */
+int b200_engine_reset(b200_engine *e);
+int64_t b200_engine_n_past(const b200_engine *e);
+
+/* Evaluates n tokens (prefill if n > 1, decode if n == 1) at positions
+ * n_past..n_past+n-1, appends their K/V and samples greedily from the last row.
+ * host_ids: host memory; host_last_logits (nullable): receives the last row [V];
+ * host_token receives the greedy token. Synchronous (like read_logits +
+ * Sampler::sample, sampler.cpp:5-65). On error nothing is committed. */
+int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n,
+                     float *host_last_logits, int32_t *host_token);
+
+/* Greedy decode of n_steps tokens entirely on the device: each step feeds the
+ * previous step's token back (CUDA-graph replay, no host round trip); the first
+ * input is the token sampled by the last eval. host_tokens (nullable) receives
+ * the n_steps generated tokens after the final synchronization. */
+int b200_engine_generate(b200_engine *e, int64_t n_steps, int32_t *host_tokens);
+
+/* Per-op timing of one decode step (CUDA events around each launch, no graph):
+ * writes up to max_ops (name, microseconds) pairs; returns the count or <0. */
+int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *us,
+                             int max_ops);
+
+/* Raw handles for in-process callers (bench / tests): the engine's stream and
+ * device status word. */
+void *b200_engine_stream(b200_engine *e);
+int b200_engine_read_status(b200_engine *e, int32_t *status);
+
+/* Tensor parallelism over NCCL: every rank calls with the same 128-byte
+ * ncclUniqueId (created by rank 0 with b200_tp_unique_id) before finalize. */
+int b200_tp_unique_id(unsigned char out_id[128]);
+int b200_engine_tp_init(b200_engine *e, const unsigned char id[128]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_INFER_H */

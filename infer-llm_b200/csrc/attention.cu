@@ -1,0 +1,432 @@
+// GQA causal attention for sm_100a over the reference's token-major KV cache
+// (element (t, h, d) at base + t*tok_stride + h*head_stride + d; the reference's
+// NaiveKVStorage object is K block then V block, naiveKVStorage.cpp:28-40).
+//
+// Semantics follow CPUBackend::compute_flash_attn (cpu_backend.cpp:555-632):
+// key j is visible to query i iff j <= n_past + i, kv_head = q_head / (Hq/Hkv),
+// softmax over the visible keys, out = sum p_j v_j. The softmax here is the
+// online (flash) form: same math, different rounding order.
+#include "attention.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kDecThreads = 128;
+constexpr int kDecTile = 32;
+
+struct DecWs {
+    unsigned *counters;  // [Hkv]
+    float *ml;           // [Hkv][S][G][2]
+    float *o;            // [Hkv][S][G][D]
+};
+
+__host__ __device__ inline DecWs dec_ws(void *base, int64_t D, int64_t Hq, int64_t Hkv, int S) {
+    DecWs w;
+    unsigned char *p = static_cast<unsigned char *>(base);
+    w.counters = reinterpret_cast<unsigned *>(p);
+    size_t off = (static_cast<size_t>(Hkv) * 4 + 255) & ~size_t(255);
+    w.ml = reinterpret_cast<float *>(p + off);
+    off += static_cast<size_t>(Hq) * S * 2 * 4;
+    off = (off + 255) & ~size_t(255);
+    w.o = reinterpret_cast<float *>(p + off);
+    (void)D;
+    return w;
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs a, const int S) {
+    constexpr int LD = D + 4;
+    constexpr int DPT = (D + kDecThreads - 1) / kDecThreads;  // dims per thread
+    extern __shared__ __align__(16) float sm[];
+    float *Ks = sm;                            // [2][32][LD]
+    float *Vs = Ks + 2 * kDecTile * LD;        // [2][32][LD]
+    float *qs = Vs + 2 * kDecTile * LD;        // [G][D]
+    float *P = qs + G * D;                     // [G][32]
+    float *alpha_s = P + G * kDecTile;         // [G]
+    __shared__ unsigned s_ticket;
+
+    grid_launch_dependents();
+    grid_wait();
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s = blockIdx.x;
+    const int64_t kvh = blockIdx.y;
+    const int64_t n_past = a.n_past_dev ? static_cast<int64_t>(*a.n_past_dev) : a.n_past;
+    const int64_t L = n_past + 1;  // Tq == 1: keys 0..n_past are visible
+    const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
+    const int ntiles = static_cast<int>((j1 - j0 + kDecTile - 1) / kDecTile);
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(D));
+
+    for (int i = tid; i < G * D; i += kDecThreads) qs[i] = a.q[(kvh * G) * D + i];
+
+    const float *kb = a.k + kvh * a.k_head;
+    const float *vb = a.v + kvh * a.v_head;
+    auto load_tile = [&](int t, int buf) {
+        const int64_t base = j0 + static_cast<int64_t>(t) * kDecTile;
+        constexpr int C4 = D / 4;
+        for (int i = tid; i < kDecTile * C4; i += kDecThreads) {
+            const int r = i / C4, c = i % C4;
+            const int64_t j = base + r;
+            const bool ok = j < j1;
+            const int64_t jj = ok ? j : j0;
+            cp_async16_zfill(Ks + (buf * kDecTile + r) * LD + c * 4, kb + jj * a.k_tok + c * 4, ok);
+            cp_async16_zfill(Vs + (buf * kDecTile + r) * LD + c * 4, vb + jj * a.v_tok + c * 4, ok);
+        }
+        cp_async_commit();
+    };
+
+    float m_run = -INFINITY, l_run = 0.f;  // valid in warp g (< G), replicated over lanes
+    float acc[G][DPT];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) acc[g][e] = 0.f;
+
+    if (ntiles > 0) load_tile(0, 0);
+    for (int t = 0; t < ntiles; ++t) {
+        const int buf = t & 1;
+        if (t + 1 < ntiles) {
+            load_tile(t + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (warp < G) {
+            const int64_t j = j0 + static_cast<int64_t>(t) * kDecTile + lane;
+            const bool valid = j < j1;
+            const float *kr = Ks + (buf * kDecTile + lane) * LD;
+            const float *qr = qs + warp * D;
+            float dot = 0.f;
+#pragma unroll 8
+            for (int k = 0; k < D; k += 4) {
+                const float4 kv = *reinterpret_cast<const float4 *>(kr + k);
+                const float4 qv = *reinterpret_cast<const float4 *>(qr + k);
+                dot = fmaf(qv.x, kv.x, dot);
+                dot = fmaf(qv.y, kv.y, dot);
+                dot = fmaf(qv.z, kv.z, dot);
+                dot = fmaf(qv.w, kv.w, dot);
+            }
+            const float sc = valid ? dot * scale : -INFINITY;
+            const float m_new = fmaxf(m_run, warp_max(sc));
+            const float p = valid ? expf(sc - m_new) : 0.f;
+            const float al = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+            l_run = l_run * al + warp_sum(p);
+            m_run = m_new;
+            P[warp * kDecTile + lane] = p;
+            if (lane == 0) alpha_s[warp] = al;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) {
+            const int d = tid + e * kDecThreads;
+            if (d < D) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float o = acc[g][e] * alpha_s[g];
+                    const float *pg = P + g * kDecTile;
+#pragma unroll 8
+                    for (int c = 0; c < kDecTile; ++c) o = fmaf(pg[c], Vs[(buf * kDecTile + c) * LD + d], o);
+                    acc[g][e] = o;
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // partials
+    DecWs w = dec_ws(a.ws, D, a.Hq, a.Hkv, S);
+    const int64_t slot = (kvh * S + s) * G;
+    if (warp < G && lane == 0) {
+        w.ml[(slot + warp) * 2 + 0] = m_run;
+        w.ml[(slot + warp) * 2 + 1] = l_run;
+    }
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) {
+        const int d = tid + e * kDecThreads;
+        if (d < D)
+#pragma unroll
+            for (int g = 0; g < G; ++g) w.o[(slot + g) * D + d] = acc[g][e];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_ticket = atomicAdd(w.counters + kvh, 1u);
+    __syncthreads();
+    if (s_ticket != static_cast<unsigned>(S - 1)) return;
+    __threadfence();
+    // Last CTA of this KV head: merge the S splits in split order.
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) {
+        const int d = tid + e * kDecThreads;
+        if (d >= D) continue;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float M = -INFINITY;
+            for (int ss = 0; ss < S; ++ss) M = fmaxf(M, __ldcg(w.ml + ((kvh * S + ss) * G + g) * 2));
+            float lsum = 0.f, o = 0.f;
+            for (int ss = 0; ss < S; ++ss) {
+                const int64_t sl = (kvh * S + ss) * G + g;
+                const float ms = __ldcg(w.ml + sl * 2);
+                if (ms == -INFINITY) continue;
+                const float f = expf(ms - M);
+                lsum = fmaf(f, __ldcg(w.ml + sl * 2 + 1), lsum);
+                o = fmaf(f, __ldcg(w.o + sl * D + d), o);
+            }
+            a.out[(kvh * G + g) * D + d] = o / lsum;
+        }
+    }
+    if (tid == 0) w.counters[kvh] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+constexpr int kPreThreads = 256;
+constexpr int kRows = 64;   // query rows (token, head) per CTA
+constexpr int kKeys = 64;   // keys per tile
+
+template <int D, int G>
+__global__ void __launch_bounds__(kPreThreads, 1) attn_prefill_kernel(const AttnArgs a) {
+    constexpr int LD = D + 4;
+    constexpr int BQ = kRows / G;       // query tokens per CTA
+    constexpr int DV = D / 16;          // output dims per thread (8 for D=128)
+    constexpr int PLD = kKeys + 4;
+    extern __shared__ __align__(16) float sm[];
+    float *Qs = sm;                     // [64][LD]
+    float *Ks = Qs + kRows * LD;        // [64][LD]
+    float *Vs = Ks + kKeys * LD;        // [64][LD]
+    float *Ps = Vs + kKeys * LD;        // [64][PLD]
+
+    grid_launch_dependents();
+    grid_wait();
+
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t qb = gridDim.x - 1 - blockIdx.x;  // heaviest blocks first
+    const int64_t kvh = blockIdx.y;
+    const int64_t q0 = qb * BQ;
+    const int64_t n_past = a.n_past_dev ? static_cast<int64_t>(*a.n_past_dev) : a.n_past;
+    const int64_t Tkv = n_past + a.Tq;
+    const int64_t kv_end = min64(Tkv, n_past + min64(q0 + BQ, a.Tq));
+    const int ntiles = static_cast<int>((kv_end + kKeys - 1) / kKeys);
+    const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(D));
+    constexpr int C4 = D / 4;
+
+    // Q rows r = tl*G + g: token q0+tl, head kvh*G+g (the G heads are contiguous)
+    for (int i = tid; i < kRows * C4; i += kPreThreads) {
+        const int r = i / C4, c = i % C4;
+        const int64_t tok = q0 + r / G;
+        const bool ok = tok < a.Tq;
+        const float *src = a.q + ((ok ? tok : 0) * a.Hq + kvh * G + (r % G)) * D + c * 4;
+        cp_async16_zfill(Qs + r * LD + c * 4, src, ok);
+    }
+    const float *kb = a.k + kvh * a.k_head;
+    const float *vb = a.v + kvh * a.v_head;
+    auto load_kv = [&](float *dst, const float *base, int64_t tok_stride, int t) {
+        for (int i = tid; i < kKeys * C4; i += kPreThreads) {
+            const int r = i / C4, c = i % C4;
+            const int64_t j = static_cast<int64_t>(t) * kKeys + r;
+            const bool ok = j < kv_end;
+            cp_async16_zfill(dst + r * LD + c * 4, base + (ok ? j : 0) * tok_stride + c * 4, ok);
+        }
+        cp_async_commit();
+    };
+
+    float m_run[4], l_run[4], o[4][DV];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m_run[i] = -INFINITY;
+        l_run[i] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DV; ++e) o[i][e] = 0.f;
+    }
+    int64_t qpos[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qpos[i] = n_past + q0 + (ty + 16 * i) / G;
+
+    if (ntiles > 0) load_kv(Ks, kb, a.k_tok, 0);  // commits Q + K0 together
+    for (int t = 0; t < ntiles; ++t) {
+        load_kv(Vs, vb, a.v_tok, t);
+        cp_async_wait<1>();
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int k = 0; k < D; k += 4) {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(Qs + (ty + 16 * i) * LD + k);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4 *>(Ks + (tx + 16 * j) * LD + k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+                }
+        }
+        float alpha[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t kpos = static_cast<int64_t>(t) * kKeys + tx + 16 * j;
+                const bool vis = kpos <= qpos[i] && kpos < Tkv;
+                sc[i][j] = vis ? sc[i][j] * scale : -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m_run[i], mx);
+            float rs = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = (sc[i][j] == -INFINITY) ? 0.f : expf(sc[i][j] - m_new);
+                sc[i][j] = p;
+                rs += p;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+            alpha[i] = (m_run[i] == -INFINITY) ? 0.f : expf(m_run[i] - m_new);
+            l_run[i] = l_run[i] * alpha[i] + rs;
+            m_run[i] = m_new;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) Ps[(ty + 16 * i) * PLD + tx + 16 * j] = sc[i][j];
+#pragma unroll
+            for (int e = 0; e < DV; ++e) o[i][e] *= alpha[i];
+        }
+        __syncthreads();  // Ks free, Ps complete
+        const bool more = t + 1 < ntiles;
+        if (more) load_kv(Ks, kb, a.k_tok, t + 1);
+        if (more) cp_async_wait<1>(); else cp_async_wait<0>();
+        __syncthreads();  // Vs ready
+#pragma unroll 4
+        for (int c = 0; c < kKeys; ++c) {
+            float4 v0 = *reinterpret_cast<const float4 *>(Vs + c * LD + tx * 4);
+            float4 v1 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (DV == 8) v1 = *reinterpret_cast<const float4 *>(Vs + c * LD + 64 + tx * 4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float p = Ps[(ty + 16 * i) * PLD + c];
+                o[i][0] = fmaf(p, v0.x, o[i][0]);
+                o[i][1] = fmaf(p, v0.y, o[i][1]);
+                o[i][2] = fmaf(p, v0.z, o[i][2]);
+                o[i][3] = fmaf(p, v0.w, o[i][3]);
+                if (DV == 8) {
+                    o[i][4 % DV] = fmaf(p, v1.x, o[i][4 % DV]);
+                    o[i][5 % DV] = fmaf(p, v1.y, o[i][5 % DV]);
+                    o[i][6 % DV] = fmaf(p, v1.z, o[i][6 % DV]);
+                    o[i][7 % DV] = fmaf(p, v1.w, o[i][7 % DV]);
+                }
+            }
+        }
+        __syncthreads();  // Vs / Ps reused next tile
+    }
+    cp_async_wait<0>();
+
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = ty + 16 * i;
+        const int64_t tok = q0 + r / G;
+        if (tok >= a.Tq) continue;
+        float *dst = a.out + (tok * a.Hq + kvh * G + (r % G)) * D;
+        const float inv = 1.0f / l_run[i];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[tx * 4 + e] = o[i][e] * inv;
+        if (DV == 8)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[64 + tx * 4 + e] = o[i][(4 + e) % DV] * inv;
+    }
+}
+
+template <int D, int G>
+cudaError_t dec_launch(const AttnArgs &a, int S, cudaStream_t stream, bool pdl) {
+    const size_t smem = (4 * kDecTile * (D + 4) + G * D + G * kDecTile + G) * sizeof(float);
+    auto kern = attn_decode_kernel<D, G>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    return b200_launch(kern, dim3(S, static_cast<unsigned>(a.Hkv)), dim3(kDecThreads), smem, stream, pdl, a, S);
+}
+
+template <int D, int G>
+cudaError_t pre_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
+    constexpr int BQ = kRows / G;
+    const size_t smem = ((kRows + 2 * kKeys) * (D + 4) + kRows * (kKeys + 4)) * sizeof(float);
+    auto kern = attn_prefill_kernel<D, G>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const dim3 grid(static_cast<unsigned>((a.Tq + BQ - 1) / BQ), static_cast<unsigned>(a.Hkv));
+    return b200_launch(kern, grid, dim3(kPreThreads), smem, stream, pdl, a);
+}
+
+template <int D>
+cudaError_t dec_by_g(const AttnArgs &a, int S, cudaStream_t st, bool pdl) {
+    switch (a.Hq / a.Hkv) {
+        case 1: return dec_launch<D, 1>(a, S, st, pdl);
+        case 2: return dec_launch<D, 2>(a, S, st, pdl);
+        case 4: return dec_launch<D, 4>(a, S, st, pdl);
+        case 8: return dec_launch<D, 8>(a, S, st, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int D>
+cudaError_t pre_by_g(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    switch (a.Hq / a.Hkv) {
+        case 1: return pre_launch<D, 1>(a, st, pdl);
+        case 2: return pre_launch<D, 2>(a, st, pdl);
+        case 4: return pre_launch<D, 4>(a, st, pdl);
+        case 8: return pre_launch<D, 8>(a, st, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+bool strides_ok(const AttnArgs &a) {
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return a.Hkv > 0 && a.Hq % a.Hkv == 0 && (a.k_tok & 3) == 0 && (a.k_head & 3) == 0 &&
+           (a.v_tok & 3) == 0 && (a.v_head & 3) == 0 && al(a.q) && al(a.k) && al(a.v);
+}
+
+}  // namespace
+
+int attn_decode_splits(int64_t max_len) {
+    // One wave of CTAs over the KV heads for long contexts, fewer for short ones.
+    int64_t s = (max_len + 63) / 64;
+    if (s < 1) s = 1;
+    if (s > 18) s = 18;
+    return static_cast<int>(s);
+}
+
+size_t attn_decode_ws_bytes(int64_t D, int64_t Hq, int64_t Hkv, int splits) {
+    size_t off = (static_cast<size_t>(Hkv) * 4 + 255) & ~size_t(255);
+    off += static_cast<size_t>(Hq) * splits * 2 * 4;
+    off = (off + 255) & ~size_t(255);
+    off += static_cast<size_t>(Hq) * splits * D * 4;
+    return off;
+}
+
+cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t stream, bool pdl) {
+    if (!strides_ok(a) || a.Tq != 1 || splits < 1) return cudaErrorInvalidValue;
+    if (a.ws_bytes < attn_decode_ws_bytes(a.D, a.Hq, a.Hkv, splits)) return cudaErrorInvalidValue;
+    switch (a.D) {
+        case 64: return dec_by_g<64>(a, splits, stream, pdl);
+        case 128: return dec_by_g<128>(a, splits, stream, pdl);
+        case 256: return dec_by_g<256>(a, splits, stream, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t attn_prefill_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
+    if (!strides_ok(a) || a.Tq < 1) return cudaErrorInvalidValue;
+    switch (a.D) {
+        case 64: return pre_by_g<64>(a, stream, pdl);
+        case 128: return pre_by_g<128>(a, stream, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace b200

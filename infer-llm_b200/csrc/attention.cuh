@@ -1,0 +1,33 @@
+// GQA causal attention over a token-major KV cache.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200 {
+
+struct AttnArgs {
+    const float *q = nullptr;   // [Tq][Hq][D]
+    const float *k = nullptr;   // element (t, h, d) at k[t*k_tok + h*k_head + d]
+    const float *v = nullptr;
+    float *out = nullptr;       // [Tq][Hq][D]
+    int64_t k_tok = 0, k_head = 0, v_tok = 0, v_head = 0;
+    int64_t D = 0, Hq = 0, Hkv = 0, Tq = 0;
+    int64_t n_past = 0;                  // host value, used when n_past_dev is null
+    const int32_t *n_past_dev = nullptr; // device scalar (graph-replayed decode)
+    float scale = 0.f;
+    void *ws = nullptr;                  // decode split partials + counters
+    size_t ws_bytes = 0;
+    int32_t *status = nullptr;
+};
+
+// Decode (Tq == 1): fixed `splits` x Hkv CTAs, each a slice of [0, n_past+1),
+// merged in-kernel by the last CTA of each KV head. Counters in `ws` must be zero
+// before the first launch (the kernel re-zeroes them).
+int attn_decode_splits(int64_t max_len);
+size_t attn_decode_ws_bytes(int64_t D, int64_t Hq, int64_t Hkv, int splits);
+cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t stream, bool pdl);
+
+// Prefill / multi-token (Tq >= 1): tiled online softmax, causal tile skipping.
+cudaError_t attn_prefill_launch(const AttnArgs &a, cudaStream_t stream, bool pdl);
+
+}  // namespace b200

@@ -1,0 +1,182 @@
+// Shared device helpers for the sm_100a kernels: bulk-copy (TMA engine) staging
+// with mbarriers, bounded waits, programmatic dependent launch, warp reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200_infer.h"
+
+#define B200_HOST_DEVICE __host__ __device__ __forceinline__
+#define B200_DEVICE __device__ __forceinline__
+
+// Upper bound on mbarrier / flag polling iterations before a wait is declared
+// stuck. At ~20 ns per try_wait round trip this is several seconds: no correct
+// run gets near it, and a stuck kernel still returns with B200_DEV_TIMEOUT.
+#define B200_SPIN_LIMIT (1u << 28)
+
+namespace b200 {
+
+B200_HOST_DEVICE int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+B200_HOST_DEVICE int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// ---------------------------------------------------------------------------
+// Status word: the first non-zero code wins.
+B200_DEVICE void set_status(int32_t *status, int32_t code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel launched with the
+// programmatic-serialization attribute calls grid_wait() before it reads data
+// produced by the previous kernel in the stream, and grid_launch_dependents()
+// as early as possible so the next kernel's CTAs can be scheduled and start
+// prefetching their (input-independent) weights.
+B200_DEVICE void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+B200_DEVICE void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + cp.async.bulk (the 1-D form of the TMA engine).
+B200_DEVICE uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+B200_DEVICE void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async proxy (bulk copies).
+B200_DEVICE void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+B200_DEVICE void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+B200_DEVICE void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+B200_DEVICE bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete. Returns false
+// (after B200_SPIN_LIMIT polls) if it never does.
+B200_DEVICE bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// Global -> shared bulk copy completing on `bar` (bytes: multiple of 16, both
+// addresses 16-byte aligned). L2 evict-first: weights are streamed once per step.
+B200_DEVICE void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar,
+                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+B200_DEVICE uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+B200_DEVICE uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Named barrier over `threads` threads (a multiple of 32) with id 1..15.
+B200_DEVICE void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Ampere-style 16-byte async copies (used where tiles are gathered row by row).
+B200_DEVICE void cp_async16(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+B200_DEVICE void cp_async16_zfill(void *smem_dst, const void *gmem_src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+B200_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+B200_DEVICE void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Streaming 128-bit load that does not allocate in L1.
+B200_DEVICE float4 ld_stream4(const float4 *p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+B200_DEVICE float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+B200_DEVICE double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+B200_DEVICE float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// RMSNorm scale with the reference's rounding (cpu_backend.cpp:369-376): squares
+// are float products accumulated in double; scale = float(1 / sqrt(mean + eps)).
+B200_DEVICE float rms_scale_from_sumsq(double sumsq, int64_t D, float eps) {
+    return static_cast<float>(1.0 / sqrt(sumsq / static_cast<double>(D) + static_cast<double>(eps)));
+}
+
+}  // namespace b200
+
+// Host-side launch helper: launch with the PDL attribute on `stream`.
+template <typename Kernel, typename... Args>
+static inline cudaError_t b200_launch(Kernel kernel, dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}

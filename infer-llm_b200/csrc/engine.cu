@@ -1,0 +1,927 @@
+// Qwen3 F32 inference engine for one B200 (or one tensor-parallel rank).
+//
+// It executes the per-step graph of Qwen3Model::build_graph (Qwen3.cpp:4-136)
+// as a fixed sequence of fused sm_100a kernels over device-resident arenas that
+// are sized once at creation (weights, KV cache, activations, workspaces), so no
+// step allocates, copies the RoPE table or synchronizes mid-step:
+//
+//   decode (per layer): [RMSNorm+QKV GEMV] [QK-norm+RoPE+KV append]
+//                       [split-KV attention + merge] [o_proj GEMV + residual]
+//                       [RMSNorm+gate/up GEMV+SwiGLU] [down GEMV + residual]
+//   then [final RMSNorm + LM head GEMV + greedy argmax (+ n_past advance)].
+//   The first layer's QKV GEMV gathers the embedding row itself.
+//
+// The decode step reads the token and n_past from device memory and writes the
+// next token back, so it is captured once as a CUDA graph and replayed with no
+// host round trip. Prefill uses the tiled FFMA / tcgen05 GEMMs and the tiled
+// attention kernel over all prompt rows and samples from the last row only.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "engine_tp.cuh"
+#include "gemm.cuh"
+#include "gemv.cuh"
+
+using namespace b200;
+
+namespace {
+
+struct LayerW {
+    float *attn_norm = nullptr, *wqkv = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    float *wo = nullptr, *ffn_norm = nullptr, *wgu = nullptr, *wdown = nullptr;
+    float *kc = nullptr, *vc = nullptr;  // KV object: K block [cap][Hkv][D], V block
+};
+
+inline int from_cuda(cudaError_t e) {
+    if (e == cudaSuccess) return B200_OK;
+    if (e == cudaErrorMemoryAllocation) return B200_ERR_NO_MEMORY;
+    if (e == cudaErrorInvalidValue) return B200_ERR_INVALID_ARGUMENT;
+    if (e == cudaErrorNotSupported) return B200_ERR_NOT_SUPPORTED;
+    return B200_ERR_CUDA;
+}
+
+#define B200_TRY(expr)                               \
+    do {                                             \
+        const cudaError_t _e = (expr);               \
+        if (_e != cudaSuccess) return from_cuda(_e); \
+    } while (0)
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3",
+// SC'11) keyed by the seed; counter = (element index, tensor id).
+__device__ __forceinline__ uint4 philox(uint4 c, uint2 k) {
+    constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+        const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+        c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+        k.x += W0;
+        k.y += W1;
+    }
+    return c;
+}
+
+// out[i] = std * N(0,1) via Box-Muller on two Philox words.
+__global__ void fill_normal_kernel(float *out, int64_t n, uint64_t seed, uint32_t tensor_id, float std) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint4 r = philox(make_uint4(static_cast<uint32_t>(i), static_cast<uint32_t>(i >> 32), tensor_id, 0u),
+                               make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32)));
+        const float u1 = (static_cast<float>(r.x >> 8) + 1.0f) * (1.0f / 16777216.0f);  // (0, 1]
+        const float u2 = static_cast<float>(r.y >> 8) * (1.0f / 16777216.0f);
+        out[i] = std * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    }
+}
+
+__global__ void fill_value_kernel(float *out, int64_t n, float v) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = v;
+}
+
+}  // namespace
+
+struct b200_engine {
+    b200_qwen3_config c{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int H = 0, D = 0, Hq = 0, Hkv = 0, F = 0, V = 0;   // per-rank sizes (Hq, Hkv, F, V sharded)
+    int64_t vocab_off = 0;                              // first vocab row of this rank's LM head
+    int qkv_rows = 0;
+    // arenas
+    unsigned char *w_arena = nullptr, *kv_arena = nullptr, *act_arena = nullptr;
+    size_t w_bytes = 0, kv_bytes = 0, act_bytes = 0;
+    std::vector<LayerW> L;
+    float *tok_embd = nullptr, *out_norm = nullptr, *lm_head = nullptr, *freq = nullptr;
+    // activations
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+    float *logits = nullptr;
+    int32_t *ids = nullptr, *token = nullptr, *n_past_dev = nullptr, *status = nullptr;
+    int32_t *token_log = nullptr, *log_pos = nullptr;
+    int32_t log_cap = 0;
+    void *attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+    int attn_splits = 1;
+    float *am_val = nullptr;
+    int32_t *am_idx = nullptr;
+    unsigned *am_counter = nullptr;
+    float *tp_pairs = nullptr;  // [world][2] (value, index) for the vocab-sharded argmax
+    // state
+    int64_t n_past = 0;
+    std::vector<std::string> missing;
+    bool finalized = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    bool graph_logits = false;
+    b200_tp *tp = nullptr;
+    int32_t *pinned_io = nullptr;  // small pinned host buffer for per-step ids / tokens
+    // per-op timing (b200_engine_profile_step): an event is recorded after each launch
+    std::vector<cudaEvent_t> *prof_events = nullptr;
+    std::vector<const char *> *prof_names = nullptr;
+};
+
+namespace {
+
+inline cudaError_t mark(b200_engine *e, const char *name, cudaError_t launched) {
+    if (launched != cudaSuccess || !e->prof_events) return launched;
+    cudaEvent_t ev;
+    cudaError_t err = cudaEventCreate(&ev);
+    if (err != cudaSuccess) return err;
+    e->prof_events->push_back(ev);
+    e->prof_names->push_back(name);
+    return cudaEventRecord(ev, e->stream);
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool parse_layer(const char *name, int *layer, const char **rest) {
+    if (std::strncmp(name, "blk.", 4) != 0) return false;
+    char *end = nullptr;
+    const long v = std::strtol(name + 4, &end, 10);
+    if (end == name + 4 || *end != '.') return false;
+    *layer = static_cast<int>(v);
+    *rest = end + 1;
+    return true;
+}
+
+// One decode step (M tokens at most 4, all from device memory) on e->stream.
+// `first_ids`: device ids for the embedding gather of layer 0.
+int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool want_logits, int n_past_add,
+                       bool pdl) {
+    cudaStream_t st = e->stream;
+    const int H = e->H, D = e->D;
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        const LayerW &w = e->L[l];
+        GemvArgs g;
+        g.w = w.wqkv;
+        g.K = H;
+        g.N = e->qkv_rows;
+        g.M = M;
+        g.gamma = w.attn_norm;
+        g.eps = e->c.rms_eps;
+        g.out = e->qkv;
+        g.epi = GEMV_STORE;
+        g.status = e->status;
+        if (l == 0) {
+            g.embed_table = e->tok_embd;
+            g.embed_ids = first_ids;
+            g.embed_rows = e->c.n_vocab;
+            g.x_store = e->x;
+        } else {
+            g.x = e->x;
+        }
+        B200_TRY(mark(e, "qkv_gemv", gemv_launch(g, st, pdl)));
+
+        QkNormRopeArgs r;
+        r.q_in = e->qkv;
+        r.q_ld = e->qkv_rows;
+        r.k_in = e->qkv + e->Hq * D;
+        r.k_ld = e->qkv_rows;
+        r.v_in = e->qkv + (e->Hq + e->Hkv) * D;
+        r.v_ld = e->qkv_rows;
+        r.q_gamma = w.q_norm;
+        r.k_gamma = w.k_norm;
+        r.freq = e->freq;
+        r.pos_base = e->n_past_dev;
+        r.out_offset = e->n_past_dev;
+        r.q_out = e->q;
+        r.k_out = w.kc;
+        r.k_out_ld = static_cast<int64_t>(e->Hkv) * D;
+        r.v_out = w.vc;
+        r.v_out_ld = static_cast<int64_t>(e->Hkv) * D;
+        r.D = D;
+        r.Hq = e->Hq;
+        r.Hkv = e->Hkv;
+        r.T = M;
+        r.n_ctx = e->c.kv_capacity;
+        r.eps = e->c.rms_eps;
+        r.status = e->status;
+        B200_TRY(mark(e, "qk_norm_rope_kv", qk_norm_rope_launch(r, st, pdl)));
+
+        AttnArgs a;
+        a.q = e->q;
+        a.k = w.kc;
+        a.v = w.vc;
+        a.out = e->attn;
+        a.k_tok = static_cast<int64_t>(e->Hkv) * D;
+        a.k_head = D;
+        a.v_tok = static_cast<int64_t>(e->Hkv) * D;
+        a.v_head = D;
+        a.D = D;
+        a.Hq = e->Hq;
+        a.Hkv = e->Hkv;
+        a.Tq = M;
+        a.n_past_dev = e->n_past_dev;
+        a.ws = e->attn_ws;
+        a.ws_bytes = e->attn_ws_bytes;
+        a.status = e->status;
+        if (M == 1)
+            B200_TRY(mark(e, "attn_decode", attn_decode_launch(a, e->attn_splits, st, pdl)));
+        else
+            B200_TRY(mark(e, "attn_prefill", attn_prefill_launch(a, st, pdl)));
+
+        GemvArgs o;
+        o.w = w.wo;
+        o.K = static_cast<int64_t>(e->Hq) * D;
+        o.N = H;
+        o.M = M;
+        o.x = e->attn;
+        o.out = e->x;
+        o.residual = e->x;
+        o.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
+        o.status = e->status;
+        B200_TRY(mark(e, "o_proj_gemv", gemv_launch(o, st, pdl)));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
+
+        GemvArgs gu;
+        gu.w = w.wgu;
+        gu.K = H;
+        gu.N = 2 * static_cast<int64_t>(e->F);
+        gu.M = M;
+        gu.x = e->x;
+        gu.gamma = w.ffn_norm;
+        gu.eps = e->c.rms_eps;
+        gu.out = e->h;
+        gu.epi = GEMV_SWIGLU;
+        gu.status = e->status;
+        B200_TRY(mark(e, "gate_up_gemv", gemv_launch(gu, st, pdl)));
+
+        GemvArgs dn;
+        dn.w = w.wdown;
+        dn.K = e->F;
+        dn.N = H;
+        dn.M = M;
+        dn.x = e->h;
+        dn.out = e->x;
+        dn.residual = e->x;
+        dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
+        dn.status = e->status;
+        B200_TRY(mark(e, "down_gemv", gemv_launch(dn, st, pdl)));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
+    }
+    GemvArgs lm;
+    lm.w = e->lm_head;
+    lm.K = H;
+    lm.N = e->V;
+    lm.M = 1;
+    lm.x = e->x + static_cast<int64_t>(M - 1) * H;
+    lm.gamma = e->out_norm;
+    lm.eps = e->c.rms_eps;
+    lm.out = want_logits ? e->logits : nullptr;
+    lm.epi = GEMV_ARGMAX;
+    lm.part_val = e->am_val;
+    lm.part_idx = e->am_idx;
+    lm.counter = e->am_counter;
+    lm.status = e->status;
+    if (e->tp) {
+        lm.argmax_out = e->am_idx + 4096;     // local winner (scratch slot)
+        lm.best_val_out = e->am_val + 4096;
+        lm.idx_offset = e->vocab_off;
+        B200_TRY(gemv_launch(lm, st, pdl));
+        B200_TRY(tp_select_token(e->tp, e->am_val + 4096, e->am_idx + 4096, e->tp_pairs, e->token, e->token_log,
+                                 e->log_pos, e->log_cap, e->n_past_dev, n_past_add, st));
+    } else {
+        lm.argmax_out = e->token;
+        lm.token_log = e->token_log;
+        lm.log_pos = e->log_pos;
+        lm.log_cap = e->log_cap;
+        lm.n_past = e->n_past_dev;
+        lm.n_past_add = n_past_add;
+        B200_TRY(mark(e, "lm_head_gemv", gemv_launch(lm, st, pdl)));
+    }
+    return B200_OK;
+}
+
+// Prefill of n > 4 tokens whose ids are already in e->ids.
+int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
+    cudaStream_t st = e->stream;
+    const int H = e->H, D = e->D;
+    const bool pdl = true;
+    B200_TRY(get_rows_launch(e->tok_embd, e->ids, e->x, H, n, e->c.n_vocab, e->status, st, pdl));
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        const LayerW &w = e->L[l];
+        B200_TRY(rms_norm_launch(e->x, w.attn_norm, e->xn, H, n, e->c.rms_eps, st, pdl));
+        GemmArgs g;
+        g.x = e->xn;
+        g.ldx = H;
+        g.w = w.wqkv;
+        g.c = e->qkv;
+        g.ldc = e->qkv_rows;
+        g.M = n;
+        g.N = e->qkv_rows;
+        g.K = H;
+        g.epi = GEMM_STORE;
+        B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(g, st, pdl) : gemm_ffma_launch(g, st, pdl));
+
+        QkNormRopeArgs r;
+        r.q_in = e->qkv;
+        r.q_ld = e->qkv_rows;
+        r.k_in = e->qkv + e->Hq * D;
+        r.k_ld = e->qkv_rows;
+        r.v_in = e->qkv + (e->Hq + e->Hkv) * D;
+        r.v_ld = e->qkv_rows;
+        r.q_gamma = w.q_norm;
+        r.k_gamma = w.k_norm;
+        r.freq = e->freq;
+        r.pos_base = e->n_past_dev;
+        r.out_offset = e->n_past_dev;
+        r.q_out = e->q;
+        r.k_out = w.kc;
+        r.k_out_ld = static_cast<int64_t>(e->Hkv) * D;
+        r.v_out = w.vc;
+        r.v_out_ld = static_cast<int64_t>(e->Hkv) * D;
+        r.D = D;
+        r.Hq = e->Hq;
+        r.Hkv = e->Hkv;
+        r.T = n;
+        r.n_ctx = e->c.kv_capacity;
+        r.eps = e->c.rms_eps;
+        r.status = e->status;
+        B200_TRY(qk_norm_rope_launch(r, st, pdl));
+
+        AttnArgs a;
+        a.q = e->q;
+        a.k = w.kc;
+        a.v = w.vc;
+        a.out = e->attn;
+        a.k_tok = static_cast<int64_t>(e->Hkv) * D;
+        a.k_head = D;
+        a.v_tok = a.k_tok;
+        a.v_head = D;
+        a.D = D;
+        a.Hq = e->Hq;
+        a.Hkv = e->Hkv;
+        a.Tq = n;
+        a.n_past_dev = e->n_past_dev;
+        a.status = e->status;
+        B200_TRY(attn_prefill_launch(a, st, pdl));
+
+        GemmArgs o;
+        o.x = e->attn;
+        o.ldx = static_cast<int64_t>(e->Hq) * D;
+        o.w = w.wo;
+        o.c = e->x;
+        o.ldc = H;
+        o.r = e->x;
+        o.M = n;
+        o.N = H;
+        o.K = static_cast<int64_t>(e->Hq) * D;
+        o.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
+        B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(o, st, pdl) : gemm_ffma_launch(o, st, pdl));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
+
+        B200_TRY(rms_norm_launch(e->x, w.ffn_norm, e->xn, H, n, e->c.rms_eps, st, pdl));
+        GemmArgs gu;
+        gu.x = e->xn;
+        gu.ldx = H;
+        gu.w = w.wgu;
+        gu.c = e->h;
+        gu.ldc = e->F;
+        gu.M = n;
+        gu.N = 2 * static_cast<int64_t>(e->F);
+        gu.K = H;
+        gu.epi = GEMM_SWIGLU;
+        B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(gu, st, pdl) : gemm_ffma_launch(gu, st, pdl));
+
+        GemmArgs dn;
+        dn.x = e->h;
+        dn.ldx = e->F;
+        dn.w = w.wdown;
+        dn.c = e->x;
+        dn.ldc = H;
+        dn.r = e->x;
+        dn.M = n;
+        dn.N = H;
+        dn.K = e->F;
+        dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
+        B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(dn, st, pdl) : gemm_ffma_launch(dn, st, pdl));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
+    }
+    GemvArgs lm;
+    lm.w = e->lm_head;
+    lm.K = H;
+    lm.N = e->V;
+    lm.M = 1;
+    lm.x = e->x + static_cast<int64_t>(n - 1) * H;
+    lm.gamma = e->out_norm;
+    lm.eps = e->c.rms_eps;
+    lm.out = want_logits ? e->logits : nullptr;
+    lm.epi = GEMV_ARGMAX;
+    lm.part_val = e->am_val;
+    lm.part_idx = e->am_idx;
+    lm.counter = e->am_counter;
+    lm.status = e->status;
+    if (e->tp) {
+        lm.argmax_out = e->am_idx + 4096;
+        lm.best_val_out = e->am_val + 4096;
+        lm.idx_offset = e->vocab_off;
+        B200_TRY(gemv_launch(lm, st, pdl));
+        B200_TRY(tp_select_token(e->tp, e->am_val + 4096, e->am_idx + 4096, e->tp_pairs, e->token, e->token_log,
+                                 e->log_pos, e->log_cap, e->n_past_dev, n, st));
+    } else {
+        lm.argmax_out = e->token;
+        lm.token_log = e->token_log;
+        lm.log_pos = e->log_pos;
+        lm.log_cap = e->log_cap;
+        lm.n_past = e->n_past_dev;
+        lm.n_past_add = n;
+        B200_TRY(gemv_launch(lm, st, pdl));
+    }
+    return B200_OK;
+}
+
+int check_status(b200_engine *e) {
+    int32_t s = 0;
+    B200_TRY(cudaMemcpyAsync(&s, e->status, 4, cudaMemcpyDeviceToHost, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    if (s == 0) return B200_OK;
+    B200_TRY(cudaMemsetAsync(e->status, 0, 4, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    if (s == B200_DEV_BAD_LOGITS) return B200_ERR_NUMERIC;
+    if (s == B200_DEV_TIMEOUT) return B200_ERR_TIMEOUT;
+    if (s == B200_DEV_BAD_TOKEN || s == B200_DEV_BAD_POSITION) return B200_ERR_OUT_OF_RANGE;
+    return B200_ERR_DEVICE_CHECK;
+}
+
+int build_graph(b200_engine *e) {
+    if (e->graph_exec) return B200_OK;
+    B200_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (rc != B200_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    B200_TRY(ce);
+    e->graph = g;
+    B200_TRY(cudaGraphInstantiate(&e->graph_exec, g, 0));
+    return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **out) {
+    if (!cfg || !out) return B200_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    const b200_qwen3_config c = *cfg;
+    const int W = c.tp_world > 0 ? c.tp_world : 1;
+    if (c.n_embd <= 0 || c.n_layer <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.head_dim <= 0 || c.n_ff <= 0 ||
+        c.n_vocab <= 0 || c.kv_capacity <= 0 || c.max_batch <= 0 || c.n_head % c.n_head_kv)
+        return B200_ERR_INVALID_ARGUMENT;
+    if (c.tp_rank < 0 || c.tp_rank >= W || c.n_head % W || c.n_head_kv % W || c.n_ff % W || c.n_vocab % W)
+        return B200_ERR_INVALID_ARGUMENT;
+    if ((c.n_embd & 3) || (c.head_dim != 64 && c.head_dim != 128) || c.kv_capacity > c.n_ctx_train)
+        return B200_ERR_NOT_SUPPORTED;
+    if (!c.tied && false) return B200_ERR_NOT_SUPPORTED;
+    DeviceGuard dg(device);
+    auto *e = new b200_engine();
+    e->c = c;
+    e->c.tp_world = W;
+    e->device = device;
+    e->H = c.n_embd;
+    e->D = c.head_dim;
+    e->Hq = c.n_head / W;
+    e->Hkv = c.n_head_kv / W;
+    e->F = c.n_ff / W;
+    e->V = c.n_vocab / W;
+    e->vocab_off = static_cast<int64_t>(c.tp_rank) * e->V;
+    e->qkv_rows = (e->Hq + 2 * e->Hkv) * e->D;
+    if (((e->F) & 3) || ((e->Hq * e->D) & 3)) {
+        delete e;
+        return B200_ERR_NOT_SUPPORTED;
+    }
+    const int64_t H = e->H, D = e->D, F = e->F, V = e->V, NL = c.n_layer;
+    const int64_t cap = c.kv_capacity, MB = c.max_batch;
+
+    // ---- weight arena: embedding (full, replicated), per-layer packed, final norm, LM head
+    const size_t A = 256;
+    size_t off = 0;
+    auto take = [&](int64_t floats) {
+        const size_t o = off;
+        off = align_up(off + static_cast<size_t>(floats) * 4, A);
+        return o;
+    };
+    const size_t o_embd = take(static_cast<int64_t>(c.n_vocab) * H);
+    const size_t o_onorm = take(H);
+    const size_t o_freq = take(D / 2);
+    size_t o_lm = 0;
+    if (!c.tied) o_lm = take(V * H);
+    std::vector<size_t> lo(NL * 8);
+    for (int64_t l = 0; l < NL; ++l) {
+        lo[l * 8 + 0] = take(H);                                   // attn_norm
+        lo[l * 8 + 1] = take(static_cast<int64_t>(e->qkv_rows) * H); // wqkv
+        lo[l * 8 + 2] = take(D);                                   // q_norm
+        lo[l * 8 + 3] = take(D);                                   // k_norm
+        lo[l * 8 + 4] = take(H * e->Hq * D);                       // wo [H][Hq*D]
+        lo[l * 8 + 5] = take(H);                                   // ffn_norm
+        lo[l * 8 + 6] = take(2 * F * H);                           // wgu interleaved
+        lo[l * 8 + 7] = take(H * F);                               // wdown [H][F]
+    }
+    e->w_bytes = off;
+    // ---- KV arena: per layer K block [cap][Hkv][D] then V block (NaiveKVStorage layout)
+    const size_t kv_layer = align_up(static_cast<size_t>(cap * e->Hkv * D) * 4, A) * 2;
+    e->kv_bytes = kv_layer * NL;
+    // ---- activation arena
+    e->attn_splits = attn_decode_splits(cap);
+    e->attn_ws_bytes = attn_decode_ws_bytes(D, e->Hq, e->Hkv, e->attn_splits);
+    off = 0;
+    const size_t o_x = take(MB * H), o_xn = take(MB * H), o_qkv = take(MB * e->qkv_rows);
+    const size_t o_q = take(MB * e->Hq * D), o_attn = take(MB * e->Hq * D), o_h = take(MB * F);
+    const size_t o_logits = take(V);
+    const size_t o_ids = take(MB), o_tok = take(4), o_np = take(4), o_st = take(4);
+    e->log_cap = 65536;
+    const size_t o_log = take(e->log_cap), o_logpos = take(4);
+    const size_t o_aws = off;
+    off = align_up(off + e->attn_ws_bytes, A);
+    const size_t o_amv = take(4096 + 64), o_ami = take(4096 + 64), o_amc = take(64);
+    const size_t o_pairs = take(2 * W + 64);
+    e->act_bytes = off;
+
+    cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaMalloc(&e->w_arena, e->w_bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&e->kv_arena, e->kv_bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&e->act_arena, e->act_bytes);
+    if (err == cudaSuccess) err = cudaMallocHost(&e->pinned_io, 4096);
+    if (err != cudaSuccess) {
+        b200_engine_destroy(e);
+        cudaGetLastError();
+        return err == cudaErrorMemoryAllocation ? B200_ERR_NO_MEMORY : B200_ERR_CUDA;
+    }
+    auto wf = [&](size_t o) { return reinterpret_cast<float *>(e->w_arena + o); };
+    auto af = [&](size_t o) { return reinterpret_cast<float *>(e->act_arena + o); };
+    auto ai = [&](size_t o) { return reinterpret_cast<int32_t *>(e->act_arena + o); };
+    e->tok_embd = wf(o_embd);
+    e->out_norm = wf(o_onorm);
+    e->freq = wf(o_freq);
+    e->lm_head = c.tied ? e->tok_embd + e->vocab_off * H : wf(o_lm);
+    e->L.resize(NL);
+    for (int64_t l = 0; l < NL; ++l) {
+        LayerW &w = e->L[l];
+        w.attn_norm = wf(lo[l * 8 + 0]);
+        w.wqkv = wf(lo[l * 8 + 1]);
+        w.q_norm = wf(lo[l * 8 + 2]);
+        w.k_norm = wf(lo[l * 8 + 3]);
+        w.wo = wf(lo[l * 8 + 4]);
+        w.ffn_norm = wf(lo[l * 8 + 5]);
+        w.wgu = wf(lo[l * 8 + 6]);
+        w.wdown = wf(lo[l * 8 + 7]);
+        w.kc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l);
+        w.vc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l + kv_layer / 2);
+    }
+    e->x = af(o_x);
+    e->xn = af(o_xn);
+    e->qkv = af(o_qkv);
+    e->q = af(o_q);
+    e->attn = af(o_attn);
+    e->h = af(o_h);
+    e->logits = af(o_logits);
+    e->ids = ai(o_ids);
+    e->token = ai(o_tok);
+    e->n_past_dev = ai(o_np);
+    e->status = ai(o_st);
+    e->token_log = ai(o_log);
+    e->log_pos = ai(o_logpos);
+    e->attn_ws = e->act_arena + o_aws;
+    e->am_val = af(o_amv);
+    e->am_idx = ai(o_ami);
+    e->am_counter = reinterpret_cast<unsigned *>(e->act_arena + o_amc);
+    e->tp_pairs = af(o_pairs);
+    err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
+    if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
+    std::vector<float> hf(D / 2);
+    b200_rope_freqs(c.rope_theta, D, hf.data());
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->freq, hf.data(), hf.size() * 4, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    if (err != cudaSuccess) {
+        b200_engine_destroy(e);
+        return B200_ERR_CUDA;
+    }
+    // weights still to be provided
+    e->missing = {"token_embd.weight", "output_norm.weight"};
+    if (!c.tied) e->missing.push_back("output.weight");
+    static const char *per_layer[] = {"attn_norm", "attn_q",   "attn_k",   "attn_v",  "attn_output", "attn_q_norm",
+                                      "attn_k_norm", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+    for (int l = 0; l < c.n_layer; ++l)
+        for (const char *p : per_layer) e->missing.push_back("blk." + std::to_string(l) + "." + p + ".weight");
+    *out = e;
+    return B200_OK;
+}
+
+void b200_engine_destroy(b200_engine *e) {
+    if (!e) return;
+    DeviceGuard dg(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->graph_exec) cudaGraphExecDestroy(e->graph_exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    if (e->tp) tp_destroy(e->tp);
+    cudaFree(e->w_arena);
+    cudaFree(e->kv_arena);
+    cudaFree(e->act_arena);
+    if (e->pinned_io) cudaFreeHost(e->pinned_io);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+int b200_engine_memory(const b200_engine *e, size_t *weights, size_t *kv, size_t *act) {
+    if (!e) return B200_ERR_INVALID_ARGUMENT;
+    if (weights) *weights = e->w_bytes;
+    if (kv) *kv = e->kv_bytes;
+    if (act) *act = e->act_bytes;
+    return B200_OK;
+}
+
+int b200_engine_set_weight(b200_engine *e, const char *name, const float *host, int64_t n) {
+    if (!e || !name || !host) return B200_ERR_INVALID_ARGUMENT;
+    if (e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    const b200_qwen3_config &c = e->c;
+    const int W = c.tp_world, r = c.tp_rank;
+    const int64_t H = e->H, D = e->D, F = e->F, V = e->V;
+    const int64_t Hq_all = c.n_head, Hkv_all = c.n_head_kv;
+    cudaStream_t st = e->stream;
+    auto h2d = [&](float *dst, const float *src, int64_t floats) {
+        return cudaMemcpyAsync(dst, src, floats * 4, cudaMemcpyHostToDevice, st);
+    };
+    // rows [row0, row0+rows) of a [N][K] host matrix into dst with pitch dpitch floats
+    auto rows2d = [&](float *dst, int64_t dpitch, const float *src, int64_t K, int64_t row0, int64_t rows) {
+        return cudaMemcpy2DAsync(dst, dpitch * 4, src + row0 * K, K * 4, K * 4, rows, cudaMemcpyHostToDevice, st);
+    };
+    cudaError_t err = cudaSuccess;
+    std::string nm(name);
+    int layer = -1;
+    const char *rest = nullptr;
+    if (nm == "token_embd.weight") {
+        if (n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
+        err = h2d(e->tok_embd, host, n);
+    } else if (nm == "output_norm.weight") {
+        if (n != H) return B200_ERR_INVALID_ARGUMENT;
+        err = h2d(e->out_norm, host, n);
+    } else if (nm == "output.weight") {
+        if (c.tied || n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
+        err = h2d(e->lm_head, host + e->vocab_off * H, V * H);
+    } else if (parse_layer(name, &layer, &rest) && layer >= 0 && layer < c.n_layer) {
+        LayerW &w = e->L[layer];
+        const std::string p(rest);
+        if (p == "attn_norm.weight" || p == "ffn_norm.weight") {
+            if (n != H) return B200_ERR_INVALID_ARGUMENT;
+            err = h2d(p[0] == 'a' ? w.attn_norm : w.ffn_norm, host, H);
+        } else if (p == "attn_q_norm.weight" || p == "attn_k_norm.weight") {
+            if (n != D) return B200_ERR_INVALID_ARGUMENT;
+            err = h2d(p[5] == 'q' ? w.q_norm : w.k_norm, host, D);
+        } else if (p == "attn_q.weight") {
+            if (n != Hq_all * D * H) return B200_ERR_INVALID_ARGUMENT;
+            err = rows2d(w.wqkv, H, host, H, r * e->Hq * D, e->Hq * D);
+        } else if (p == "attn_k.weight" || p == "attn_v.weight") {
+            if (n != Hkv_all * D * H) return B200_ERR_INVALID_ARGUMENT;
+            float *dst = w.wqkv + (e->Hq + (p[5] == 'k' ? 0 : e->Hkv)) * D * H;
+            err = rows2d(dst, H, host, H, r * e->Hkv * D, e->Hkv * D);
+        } else if (p == "attn_output.weight") {
+            // [H][Hq*D]: keep this rank's column block (row-split for tensor parallelism)
+            if (n != H * Hq_all * D) return B200_ERR_INVALID_ARGUMENT;
+            const int64_t kc = e->Hq * D;
+            err = cudaMemcpy2DAsync(w.wo, kc * 4, host + r * kc, Hq_all * D * 4, kc * 4, H, cudaMemcpyHostToDevice, st);
+        } else if (p == "ffn_gate.weight" || p == "ffn_up.weight") {
+            // interleave: packed row 2i = gate row i, 2i+1 = up row i
+            if (n != static_cast<int64_t>(c.n_ff) * H) return B200_ERR_INVALID_ARGUMENT;
+            float *dst = w.wgu + (p[4] == 'g' ? 0 : H);
+            err = cudaMemcpy2DAsync(dst, 2 * H * 4, host + r * F * H, H * 4, H * 4, F, cudaMemcpyHostToDevice, st);
+        } else if (p == "ffn_down.weight") {
+            if (n != H * static_cast<int64_t>(c.n_ff)) return B200_ERR_INVALID_ARGUMENT;
+            err = cudaMemcpy2DAsync(w.wdown, F * 4, host + r * F, static_cast<int64_t>(c.n_ff) * 4, F * 4, H,
+                                    cudaMemcpyHostToDevice, st);
+        } else {
+            return B200_ERR_INVALID_ARGUMENT;
+        }
+    } else {
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);  // host buffer may be released after return
+    if (err != cudaSuccess) return from_cuda(err);
+    for (size_t i = 0; i < e->missing.size(); ++i)
+        if (e->missing[i] == nm) {
+            e->missing.erase(e->missing.begin() + i);
+            break;
+        }
+    return B200_OK;
+}
+
+int b200_engine_init_random(b200_engine *e, uint64_t seed, float std) {
+    if (!e || e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    cudaStream_t st = e->stream;
+    const int64_t H = e->H, D = e->D, F = e->F;
+    uint32_t id = 1;
+    auto normal = [&](float *p, int64_t n) {
+        fill_normal_kernel<<<1184, 256, 0, st>>>(p, n, seed + 0x9E3779B97F4A7C15ull * e->c.tp_rank, id++, std);
+        return cudaGetLastError();
+    };
+    auto ones = [&](float *p, int64_t n) {
+        fill_value_kernel<<<296, 256, 0, st>>>(p, n, 1.0f);
+        return cudaGetLastError();
+    };
+    // Shards are generated per rank (each rank's weights are its own draw); the
+    // embedding table is replicated, so it uses the rank-independent stream.
+    fill_normal_kernel<<<1184, 256, 0, st>>>(e->tok_embd, static_cast<int64_t>(e->c.n_vocab) * H, seed, 0u, std);
+    B200_TRY(cudaGetLastError());
+    B200_TRY(ones(e->out_norm, H));
+    if (!e->c.tied) B200_TRY(normal(e->lm_head, static_cast<int64_t>(e->V) * H));
+    for (auto &w : e->L) {
+        B200_TRY(ones(w.attn_norm, H));
+        B200_TRY(ones(w.ffn_norm, H));
+        B200_TRY(ones(w.q_norm, D));
+        B200_TRY(ones(w.k_norm, D));
+        B200_TRY(normal(w.wqkv, static_cast<int64_t>(e->qkv_rows) * H));
+        B200_TRY(normal(w.wo, H * e->Hq * D));
+        B200_TRY(normal(w.wgu, 2 * F * H));
+        B200_TRY(normal(w.wdown, H * F));
+    }
+    B200_TRY(cudaStreamSynchronize(st));
+    e->missing.clear();
+    return B200_OK;
+}
+
+int b200_engine_finalize(b200_engine *e) {
+    if (!e) return B200_ERR_INVALID_ARGUMENT;
+    if (!e->missing.empty()) {
+        std::fprintf(stderr, "b200_engine_finalize: %zu weights missing (first: %s)\n", e->missing.size(),
+                     e->missing[0].c_str());
+        return B200_ERR_INVALID_ARGUMENT;
+    }
+    if (e->c.tp_world > 1 && !e->tp) return B200_ERR_INVALID_ARGUMENT;
+    e->finalized = true;
+    return B200_OK;
+}
+
+int b200_engine_reset(b200_engine *e) {
+    if (!e) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    B200_TRY(cudaMemsetAsync(e->n_past_dev, 0, 4, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    e->n_past = 0;
+    return B200_OK;
+}
+
+int64_t b200_engine_n_past(const b200_engine *e) { return e ? e->n_past : -1; }
+
+int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *host_last_logits,
+                     int32_t *host_token) {
+    if (!e || !host_ids || n <= 0) return B200_ERR_INVALID_ARGUMENT;
+    if (!e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    if (n > e->c.max_batch) return B200_ERR_INVALID_ARGUMENT;
+    if (e->n_past + n > e->c.kv_capacity) return B200_ERR_OUT_OF_RANGE;
+    for (int64_t i = 0; i < n; ++i)
+        if (host_ids[i] < 0 || host_ids[i] >= e->c.n_vocab) return B200_ERR_OUT_OF_RANGE;
+    DeviceGuard dg(e->device);
+    cudaStream_t st = e->stream;
+    const bool want_logits = host_last_logits != nullptr;
+    int rc;
+    if (n == 1 && !want_logits && e->c.tp_world == 1) {
+        // graph-replayed decode: the token slot is the embedding input
+        e->pinned_io[0] = host_ids[0];
+        B200_TRY(cudaMemcpyAsync(e->token, e->pinned_io, 4, cudaMemcpyHostToDevice, st));
+        rc = build_graph(e);
+        if (rc != B200_OK) return rc;
+        B200_TRY(cudaGraphLaunch(e->graph_exec, st));
+    } else {
+        std::memcpy(e->pinned_io, host_ids, n * 4);
+        B200_TRY(cudaMemcpyAsync(e->ids, e->pinned_io, n * 4, cudaMemcpyHostToDevice, st));
+        if (n <= 4)
+            rc = enqueue_small_step(e, e->ids, static_cast<int>(n), want_logits, static_cast<int>(n), true);
+        else
+            rc = enqueue_prefill(e, static_cast<int>(n), want_logits);
+        if (rc != B200_OK) return rc;
+    }
+    B200_TRY(cudaMemcpyAsync(e->pinned_io + 1024, e->token, 4, cudaMemcpyDeviceToHost, st));
+    if (want_logits && e->c.tp_world == 1)
+        B200_TRY(cudaMemcpyAsync(host_last_logits, e->logits, static_cast<size_t>(e->V) * 4, cudaMemcpyDeviceToHost, st));
+    rc = check_status(e);  // synchronizes
+    if (rc != B200_OK) {
+        // nothing committed: restore n_past
+        const int32_t np = static_cast<int32_t>(e->n_past);
+        cudaMemcpy(e->n_past_dev, &np, 4, cudaMemcpyHostToDevice);
+        return rc;
+    }
+    if (host_token) *host_token = e->pinned_io[1024];
+    e->n_past += n;
+    return B200_OK;
+}
+
+int b200_engine_generate(b200_engine *e, int64_t n_steps, int32_t *host_tokens) {
+    if (!e || n_steps < 0 || !e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    if (e->n_past + n_steps > e->c.kv_capacity) return B200_ERR_OUT_OF_RANGE;
+    if (n_steps > e->log_cap) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    cudaStream_t st = e->stream;
+    int rc = B200_OK;
+    if (e->c.tp_world == 1) {
+        rc = build_graph(e);
+        if (rc != B200_OK) return rc;
+    }
+    B200_TRY(cudaMemsetAsync(e->log_pos, 0, 4, st));
+    for (int64_t i = 0; i < n_steps; ++i) {
+        if (e->c.tp_world == 1) {
+            B200_TRY(cudaGraphLaunch(e->graph_exec, st));
+        } else {
+            rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+            if (rc != B200_OK) return rc;
+        }
+    }
+    if (host_tokens && n_steps > 0)
+        B200_TRY(cudaMemcpyAsync(host_tokens, e->token_log, n_steps * 4, cudaMemcpyDeviceToHost, st));
+    rc = check_status(e);
+    if (rc != B200_OK) return rc;
+    e->n_past += n_steps;
+    return B200_OK;
+}
+
+int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *us, int max_ops) {
+    if (!e || !e->finalized || !names || !us || max_ops <= 0 || name_len <= 1) return B200_ERR_INVALID_ARGUMENT;
+    if (e->tp || e->n_past + 1 > e->c.kv_capacity) return B200_ERR_NOT_SUPPORTED;
+    DeviceGuard dg(e->device);
+    cudaStream_t st = e->stream;
+    // One eager decode step (no graph, no programmatic overlap) with an event after
+    // every launch. n_past and the token slot are restored afterwards, so the step
+    // leaves no trace beyond a KV row that the next real step overwrites.
+    int32_t saved[2];
+    B200_TRY(cudaMemcpyAsync(&saved[0], e->n_past_dev, 4, cudaMemcpyDeviceToHost, st));
+    B200_TRY(cudaMemcpyAsync(&saved[1], e->token, 4, cudaMemcpyDeviceToHost, st));
+    std::vector<cudaEvent_t> evs;
+    std::vector<const char *> nms;
+    cudaEvent_t start;
+    B200_TRY(cudaEventCreate(&start));
+    B200_TRY(cudaEventRecord(start, st));
+    e->prof_events = &evs;
+    e->prof_names = &nms;
+    const int rc = enqueue_small_step(e, e->token, 1, false, 1, false);
+    e->prof_events = nullptr;
+    e->prof_names = nullptr;
+    cudaError_t err = cudaStreamSynchronize(st);
+    std::vector<std::string> uniq;
+    std::vector<float> tot;
+    cudaEvent_t prev = start;
+    for (size_t i = 0; i < evs.size() && err == cudaSuccess; ++i) {
+        float ms = 0.f;
+        err = cudaEventElapsedTime(&ms, prev, evs[i]);
+        prev = evs[i];
+        size_t k = 0;
+        while (k < uniq.size() && uniq[k] != nms[i]) ++k;
+        if (k == uniq.size()) {
+            uniq.push_back(nms[i]);
+            tot.push_back(0.f);
+        }
+        tot[k] += ms * 1000.f;
+    }
+    for (auto ev : evs) cudaEventDestroy(ev);
+    cudaEventDestroy(start);
+    cudaMemcpyAsync(e->n_past_dev, &saved[0], 4, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(e->token, &saved[1], 4, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+    if (rc != B200_OK) return rc;
+    if (err != cudaSuccess) return from_cuda(err);
+    const int n = static_cast<int>(uniq.size() < static_cast<size_t>(max_ops) ? uniq.size() : max_ops);
+    for (int i = 0; i < n; ++i) {
+        std::strncpy(names + static_cast<size_t>(i) * name_len, uniq[i].c_str(), name_len - 1);
+        names[static_cast<size_t>(i) * name_len + name_len - 1] = 0;
+        us[i] = tot[i];
+    }
+    return n;
+}
+
+void *b200_engine_stream(b200_engine *e) { return e ? e->stream : nullptr; }
+
+int b200_engine_read_status(b200_engine *e, int32_t *status) {
+    if (!e || !status) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    B200_TRY(cudaMemcpy(status, e->status, 4, cudaMemcpyDeviceToHost));
+    return B200_OK;
+}
+
+int b200_tp_unique_id(unsigned char out_id[128]) { return tp_unique_id(out_id); }
+
+int b200_engine_tp_init(b200_engine *e, const unsigned char id[128]) {
+    if (!e || !id || e->c.tp_world < 2) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    return tp_create(&e->tp, id, e->c.tp_rank, e->c.tp_world);
+}
+
+}  // extern "C"

@@ -1,0 +1,31 @@
+// Prefill matrix products C[M][N] = X[M][K] . W[N][K]^T with fused epilogues.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200 {
+
+enum GemmEpi : int {
+    GEMM_STORE = 0,
+    GEMM_RESIDUAL = 1,  // C = X.W^T + R (R may alias C)
+    GEMM_SWIGLU = 2,    // W rows interleaved (gate_i, up_i): C[:, i] = up * silu(gate)
+};
+
+struct GemmArgs {
+    const float *x = nullptr;  // [M][ldx]
+    int64_t ldx = 0;
+    const float *w = nullptr;  // [N][K]
+    float *c = nullptr;        // [M][ldc]
+    int64_t ldc = 0;
+    const float *r = nullptr;  // residual [M][ldc]
+    int64_t M = 0, N = 0, K = 0;
+    int epi = GEMM_STORE;
+};
+
+// Exact F32 FFMA tiled GEMM (any M; K % 4 == 0).
+cudaError_t gemm_ffma_launch(const GemmArgs &a, cudaStream_t stream, bool pdl);
+// tcgen05 TF32 tensor-core GEMM (TMEM accumulators, bulk-staged operands).
+// Returns cudaErrorNotSupported for shapes it does not cover.
+cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl);
+
+}  // namespace b200

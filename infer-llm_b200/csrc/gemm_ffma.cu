@@ -1,0 +1,190 @@
+// Exact F32 (FFMA) tiled GEMM for prefill: C[M][N] = X[M][K] . W[N][K]^T.
+//
+// 256 threads, tile BM x 128 x 16, each thread owns a (BM/16) x 8 block of C
+// split into two column quads 64 apart so shared-memory reads are conflict free.
+// Global tiles are read with 128-bit loads into registers one K-step ahead and
+// stored transposed into a double-buffered shared tile. Epilogues fuse the
+// residual add and SwiGLU of the reference graph (Qwen3.cpp:97,109-118).
+#include "gemm.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int BN = 128, BK = 16, PAD = 4, NT = 256;
+
+template <int BM, int EPI>
+__global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
+    constexpr int TM = BM / 16;              // rows per thread
+    constexpr int A_LD = (BM * BK / 4) / NT; // float4 loads of X per thread (BM=32 -> 0.5)
+    __shared__ __align__(16) float As[2][BK][BM + PAD];
+    __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+
+    grid_launch_dependents();
+    grid_wait();
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+    const int64_t K = a.K;
+
+    // X tile: BM rows x 4 float4; W tile: 128 rows x 4 float4 (2 per thread)
+    float4 ra[A_LD > 0 ? A_LD : 1], rb[2];
+    auto load_tiles = [&](int64_t k0) {
+        if (A_LD > 0) {
+#pragma unroll
+            for (int i = 0; i < A_LD; ++i) {
+                const int f = tid + i * NT;
+                const int row = f >> 2, k4 = f & 3;
+                const int64_t gm = m0 + row, gk = k0 + k4 * 4;
+                ra[i] = (gm < a.M && gk < K) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        } else if (tid < BM * 4) {
+            const int row = tid >> 2, k4 = tid & 3;
+            const int64_t gm = m0 + row, gk = k0 + k4 * 4;
+            ra[0] = (gm < a.M && gk < K) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int f = tid + i * NT;
+            const int row = f >> 2, k4 = f & 3;
+            const int64_t gn = n0 + row, gk = k0 + k4 * 4;
+            rb[i] = (gn < a.N && gk < K) ? ld_stream4(reinterpret_cast<const float4 *>(a.w + gn * K + gk))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_tiles = [&](int buf) {
+        if (A_LD > 0) {
+#pragma unroll
+            for (int i = 0; i < A_LD; ++i) {
+                const int f = tid + i * NT;
+                const int row = f >> 2, k4 = f & 3;
+                As[buf][k4 * 4 + 0][row] = ra[i].x;
+                As[buf][k4 * 4 + 1][row] = ra[i].y;
+                As[buf][k4 * 4 + 2][row] = ra[i].z;
+                As[buf][k4 * 4 + 3][row] = ra[i].w;
+            }
+        } else if (tid < BM * 4) {
+            const int row = tid >> 2, k4 = tid & 3;
+            As[buf][k4 * 4 + 0][row] = ra[0].x;
+            As[buf][k4 * 4 + 1][row] = ra[0].y;
+            As[buf][k4 * 4 + 2][row] = ra[0].z;
+            As[buf][k4 * 4 + 3][row] = ra[0].w;
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int f = tid + i * NT;
+            const int row = f >> 2, k4 = f & 3;
+            Bs[buf][k4 * 4 + 0][row] = rb[i].x;
+            Bs[buf][k4 * 4 + 1][row] = rb[i].y;
+            Bs[buf][k4 * 4 + 2][row] = rb[i].z;
+            Bs[buf][k4 * 4 + 3][row] = rb[i].w;
+        }
+    };
+
+    float acc[TM][8];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    // rows owned: TM=8 -> {ty*4..+3} U {BM/2 + ty*4..+3}; TM=4 -> ty*4..+3; TM=2 -> ty*2..+1
+    auto row_of = [&](int i) -> int {
+        if (TM == 8) return (i < 4) ? ty * 4 + i : BM / 2 + ty * 4 + (i - 4);
+        return ty * TM + i;
+    };
+
+    const int64_t nk = (K + BK - 1) / BK;
+    load_tiles(0);
+    store_tiles(0);
+    __syncthreads();
+    for (int64_t kt = 0; kt < nk; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load_tiles((kt + 1) * BK);
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            float av[TM], bv[8];
+            if (TM == 8) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 4]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][k][BM / 2 + ty * 4]);
+                av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+                av[4 % TM] = a1.x; av[5 % TM] = a1.y; av[6 % TM] = a1.z; av[7 % TM] = a1.w;
+            } else if (TM == 4) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 4]);
+                av[0] = a0.x; av[1 % TM] = a0.y; av[2 % TM] = a0.z; av[3 % TM] = a0.w;
+            } else {
+                const float2 a0 = *reinterpret_cast<const float2 *>(&As[buf][k][ty * 2]);
+                av[0] = a0.x; av[1 % TM] = a0.y;
+            }
+            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][k][64 + tx * 4]);
+            bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+            bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (kt + 1 < nk) {
+            store_tiles(buf ^ 1);
+        }
+        __syncthreads();
+    }
+
+    // epilogue
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int64_t gm = m0 + row_of(i);
+        if (gm >= a.M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t gn = n0 + h * 64 + tx * 4;
+            if (EPI == GEMM_SWIGLU) {
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    const int64_t col = gn + 2 * p;
+                    if (col + 1 < a.N) {
+                        const float g = acc[i][h * 4 + 2 * p], u = acc[i][h * 4 + 2 * p + 1];
+                        const float sg = g / (1.0f + expf(-g));
+                        a.c[gm * a.ldc + col / 2] = u * sg;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t col = gn + j;
+                    if (col < a.N) {
+                        float v = acc[i][h * 4 + j];
+                        if (EPI == GEMM_RESIDUAL) v = v + a.r[gm * a.ldc + col];
+                        a.c[gm * a.ldc + col] = v;
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <int BM>
+cudaError_t launch_bm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+    dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + BM - 1) / BM));
+    switch (a.epi) {
+        case GEMM_STORE: return b200_launch(sgemm_kernel<BM, GEMM_STORE>, grid, dim3(NT), 0, stream, pdl, a);
+        case GEMM_RESIDUAL: return b200_launch(sgemm_kernel<BM, GEMM_RESIDUAL>, grid, dim3(NT), 0, stream, pdl, a);
+        case GEMM_SWIGLU: return b200_launch(sgemm_kernel<BM, GEMM_SWIGLU>, grid, dim3(NT), 0, stream, pdl, a);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t gemm_ffma_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0 || (a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;
+    if (a.epi == GEMM_SWIGLU && (a.N & 1)) return cudaErrorInvalidValue;
+    if (a.M <= 32) return launch_bm<32>(a, stream, pdl);
+    if (a.M <= 64) return launch_bm<64>(a, stream, pdl);
+    return launch_bm<128>(a, stream, pdl);
+}
+
+}  // namespace b200

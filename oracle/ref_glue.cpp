@@ -1,0 +1,335 @@
+// oracle/ref_glue.cpp -- TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+//
+// A thin extern "C" surface over the Infer-LLM reference engine, compiled
+// together with the reference's own sources (see oracle/Makefile). It lets the
+// Python tests and bench.py's reference leg call:
+//   * single reference CPU ops (a Graph with one OpFactory node executed by
+//     CPUBackend::compute), the checker that pins oracle/cpu_ops.c, and
+//   * the reference end-to-end CPU path: GGUF load, Qwen3Model::build_graph,
+//     Scheduler::execute, read_logits and the greedy Sampler, with the request
+//     loop of benchmarks/cpu/bench.cpp (Runner::evaluate, bench.cpp:177-219).
+// Nothing in the product library links or calls this file.
+
+#include "backend.hpp"
+#include "backends/cpu_backend.hpp"
+#include "gguf_parser.hpp"
+#include "graph.hpp"
+#include "model.hpp"
+#include "op_factory.hpp"
+#include "sampler.hpp"
+#include "scheduler.hpp"
+#include "kvcache/kvcacheManager.hpp"
+#include "kvcache/KVStorages/naiveKVStorage.hpp"
+#include "kvcache/KVStrategys/contiguousKVStrategy.hpp"
+
+#include <cstdlib>
+#include <cstring>
+#include <iostream>
+#include <memory>
+#include <numeric>
+#include <streambuf>
+#include <string>
+#include <vector>
+
+namespace {
+
+// The reference engine prints progress to std::cout on every call; the glue
+// silences it for the duration of each call (as bench.cpp:110-119 does).
+class Quiet {
+    struct Sink : std::streambuf {
+        int_type overflow(int_type c) override { return traits_type::not_eof(c); }
+        std::streamsize xsputn(const char *, std::streamsize n) override { return n; }
+    } sink_;
+    std::streambuf *old_;
+
+public:
+    Quiet() : old_(std::cout.rdbuf(&sink_)) {}
+    ~Quiet() { std::cout.rdbuf(old_); }
+};
+
+std::unique_ptr<Backend> g_cpu;
+int g_cpu_threads = -1;
+
+Backend *cpu_backend(int threads) {
+    if (g_cpu && (threads <= 0 || threads == g_cpu_threads)) return g_cpu.get();
+    Quiet q;
+    if (threads > 0) setenv("INFERLLM_THREADS", std::to_string(threads).c_str(), 1);
+    static bool registered = false;
+    if (!registered) {
+        register_all_backends();
+        registered = true;
+    }
+    auto &reg = BackendRegistry::instance();
+    reg.probe_all();
+    g_cpu.reset();
+    auto b = reg.create("cpu", PoolConfig{});
+    if (!b) return nullptr;
+    g_cpu = std::move(*b);
+    g_cpu_threads = static_cast<const CPUBackend *>(g_cpu.get())->get_n_threads();
+    return g_cpu.get();
+}
+
+Tensor *leaf(Graph &g, const char *name, DataType type, std::initializer_list<int64_t> shape,
+             const void *data, Backend *b) {
+    auto t = std::make_unique<Tensor>(name, type, shape);
+    t->data = const_cast<void *>(data);
+    t->backend = b;
+    t->device = DeviceType::CPU;
+    return g.add_node(std::move(t));
+}
+
+int run_one(Graph &g, Tensor *out, void *out_data, Backend *b) {
+    out->data = out_data;
+    out->backend = b;
+    g.mark_output(out);
+    if (!g.compute()) return -2;
+    if (!b->compute(g)) return -3;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ref_set_threads(int threads) {
+    Backend *b = cpu_backend(threads);
+    return b ? g_cpu_threads : -1;
+}
+
+int ref_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *W = leaf(g, "w", GGML_TYPE_F32, {K, N}, w, b);
+    Tensor *X = leaf(g, "x", GGML_TYPE_F32, {K, M}, x, b);
+    return run_one(g, OpFactory::mul_mat(g, W, X), out, b);
+}
+
+int ref_rms_norm(const float *x, const float *gamma, float *out, int64_t D, int64_t rows, float eps) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *X = leaf(g, "x", GGML_TYPE_F32, {D, rows}, x, b);
+    Tensor *G = leaf(g, "gamma", GGML_TYPE_F32, {D}, gamma, b);
+    return run_one(g, OpFactory::rms_norm(g, X, G, eps), out, b);
+}
+
+// Copies the reference's own host RoPE angle table (GraphContext, graph.cpp:92-135).
+int ref_rope_theta_table(float theta, uint32_t head_dim, uint32_t n_ctx, float *out) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    GraphContext ctx(b);
+    auto t = ctx.get_rope_theta_table(theta, head_dim, n_ctx);
+    if (!t) return -2;
+    std::memcpy(out, (*t)->data, sizeof(float) * (head_dim / 2) * static_cast<size_t>(n_ctx));
+    return 0;
+}
+
+int ref_rope(const float *x, const int32_t *pos, float theta, uint32_t n_ctx, float *out,
+             int64_t D, int64_t H, int64_t T) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    GraphContext ctx(b);
+    auto table = ctx.get_rope_theta_table(theta, static_cast<uint32_t>(D), n_ctx);
+    if (!table) return -2;
+    Graph g;
+    Tensor *X = leaf(g, "x", GGML_TYPE_F32, {D, H, T}, x, b);
+    Tensor *P = leaf(g, "pos", GGML_TYPE_I32, {T}, pos, b);
+    return run_one(g, OpFactory::rope(g, X, P, *table), out, b);
+}
+
+int ref_flash_attn(const float *qp, const float *kp, const float *vp, float *out, int64_t D,
+                   int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *Q = leaf(g, "q", GGML_TYPE_F32, {D, Hq, Tq}, qp, b);
+    Tensor *K = leaf(g, "k", GGML_TYPE_F32, {D, Hkv, Tkv}, kp, b);
+    Tensor *V = leaf(g, "v", GGML_TYPE_F32, {D, Hkv, Tkv}, vp, b);
+    AttnParams p;
+    p.n_head = static_cast<uint32_t>(Hq);
+    p.n_head_kv = static_cast<uint32_t>(Hkv);
+    p.head_dim = static_cast<uint32_t>(D);
+    p.scale = 1.0f / std::sqrt(float(D));
+    p.causal = true;
+    p.n_ctx = static_cast<uint32_t>(n_past);
+    return run_one(g, OpFactory::flash_attn(g, Q, K, V, p), out, b);
+}
+
+int ref_silu(const float *x, float *out, int64_t n) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *X = leaf(g, "x", GGML_TYPE_F32, {n}, x, b);
+    return run_one(g, OpFactory::silu(g, X), out, b);
+}
+
+int ref_binary(int op, const float *a, const float *bb, float *out, int64_t n) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *A = leaf(g, "a", GGML_TYPE_F32, {n}, a, b);
+    Tensor *B = leaf(g, "b", GGML_TYPE_F32, {n}, bb, b);
+    return run_one(g, op == 0 ? OpFactory::add(g, A, B) : OpFactory::mul(g, A, B), out, b);
+}
+
+int ref_get_rows(const float *table, const int32_t *ids, float *out, int64_t D, int64_t n,
+                 int64_t n_rows) {
+    Backend *b = cpu_backend(0);
+    if (!b) return -1;
+    Quiet q;
+    Graph g;
+    Tensor *T = leaf(g, "table", GGML_TYPE_F32, {D, n_rows}, table, b);
+    Tensor *I = leaf(g, "ids", GGML_TYPE_I32, {n}, ids, b);
+    return run_one(g, OpFactory::embedding(g, T, I), out, b);
+}
+
+int32_t ref_sample_greedy(const float *logits, int64_t n) {
+    Sampler s;
+    auto r = s.sample(std::span<const float>(logits, static_cast<size_t>(n)));
+    return r ? *r : -1;
+}
+
+// ---------------------------------------------------------------------------
+// End-to-end reference CPU engine (one sequence at a time).
+
+struct RefEngine {
+    std::unique_ptr<ModelBase> model;
+    std::unique_ptr<KVCacheManager> cache;
+    std::unique_ptr<GraphContext> ctx;
+    std::vector<Backend *> devices;
+    std::unique_ptr<Scheduler> scheduler;
+    SequenceId seq = kInvalidSequenceId;
+    Tensor *tokens = nullptr, *pos = nullptr;
+    std::vector<int32_t> ids, positions;
+    int64_t n_vocab = 0;
+};
+
+void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
+    Backend *b = cpu_backend(threads);
+    if (!b) return nullptr;
+    Quiet q;
+    auto gguf = GGUFContext::load(gguf_path);
+    if (!gguf) return nullptr;
+    auto arch = gguf->metadata().get_meta<std::string>("general.architecture");
+    if (!arch) return nullptr;
+    auto n_layer = gguf->metadata().get_meta<uint32_t>(*arch + ".block_count");
+    auto kv_heads = gguf->metadata().get_meta<uint32_t>(*arch + ".attention.head_count_kv");
+    auto kd = gguf->metadata().get_meta<uint32_t>(*arch + ".attention.key_length");
+    auto vd = gguf->metadata().get_meta<uint32_t>(*arch + ".attention.value_length");
+    if (!n_layer || !kv_heads || !kd || !vd) return nullptr;
+    static bool models_registered = false;
+    if (!models_registered) {
+        register_all_models();
+        models_registered = true;
+    }
+    auto e = std::make_unique<RefEngine>();
+    auto model = ModelBase::load_model(std::move(*gguf));
+    if (!model) return nullptr;
+    e->model = std::move(*model);
+    if (!e->model->load_hparams() || !e->model->load_weight()) return nullptr;
+    e->devices = {b};
+    PlacementConfig placement;
+    placement.n_ctx = static_cast<uint32_t>(capacity);
+    if (!e->model->plan_weights_placement(e->devices, placement)) return nullptr;
+    std::vector<KVLayerSpec> layers(*n_layer, KVLayerSpec{.n_kv_heads = *kv_heads,
+                                                           .k_head_dim = *kd,
+                                                           .v_head_dim = *vd,
+                                                           .k_type = GGML_TYPE_F32,
+                                                           .v_type = GGML_TYPE_F32});
+    e->cache = std::make_unique<KVCacheManager>(
+        std::make_unique<ContiguousKVStrategy>(std::make_unique<NaiveKVStorage>()));
+    std::vector<Backend *> placement_layers(layers.size(), b);
+    KVCacheConfig config{.layers = layers.size(), .max_tokens_per_sequence = static_cast<size_t>(capacity)};
+    if (!e->cache->init(layers, placement_layers, config)) return nullptr;
+    e->ctx = std::make_unique<GraphContext>(b);
+    e->scheduler = std::make_unique<Scheduler>(e->devices);
+    e->tokens = e->ctx->make_tensor("bench_tokens", DataType::GGML_TYPE_I32, {1});
+    e->pos = e->ctx->make_tensor("bench_positions", DataType::GGML_TYPE_I32, {1});
+    for (Tensor *t : {e->tokens, e->pos}) {
+        t->tensorRole = TensorRole::TNESOR_ROLE_INPUT;
+        t->backend = b;
+        t->device = DeviceType::CPU;
+    }
+    e->ctx->set_input_tokens(e->tokens);
+    e->ctx->set_input_pos(e->pos);
+    auto seq = e->cache->create_sequence();
+    if (!seq) return nullptr;
+    e->seq = *seq;
+    if (!e->ctx->set_kv_cache(e->cache.get(), e->seq)) return nullptr;
+    return e.release();
+}
+
+void ref_engine_destroy(void *h) {
+    auto *e = static_cast<RefEngine *>(h);
+    if (!e) return;
+    Quiet q;
+    (void)e->ctx->release_kv_access();
+    if (e->seq != kInvalidSequenceId) (void)e->cache->release_sequence(e->seq);
+    delete e;
+}
+
+// Starts a new request: drops the sequence's KV and creates a fresh one.
+int ref_engine_reset(void *h) {
+    auto *e = static_cast<RefEngine *>(h);
+    Quiet q;
+    if (!e->ctx->release_kv_access()) return -1;
+    if (!e->cache->release_sequence(e->seq)) return -1;
+    if (!e->ctx->set_kv_cache(nullptr, kInvalidSequenceId)) return -1;
+    auto seq = e->cache->create_sequence();
+    if (!seq) return -1;
+    e->seq = *seq;
+    if (!e->ctx->set_kv_cache(e->cache.get(), e->seq)) return -1;
+    return 0;
+}
+
+// One evaluation step (prefill when n > 1, decode when n == 1), the body of
+// bench.cpp Runner::evaluate. Writes the last row's logits (if non-null) and
+// returns the greedy token, or a negative code.
+int32_t ref_engine_eval(void *h, const int32_t *ids, int64_t n, float *last_logits) {
+    auto *e = static_cast<RefEngine *>(h);
+    Quiet q;
+    auto n_past = e->cache->length(e->seq);
+    if (!n_past) return -1;
+    if (!e->cache->reserve_append(e->seq, static_cast<size_t>(n))) return -2;
+    e->ids.assign(ids, ids + n);
+    e->positions.resize(static_cast<size_t>(n));
+    std::iota(e->positions.begin(), e->positions.end(), static_cast<int32_t>(*n_past));
+    const int64_t bytes = n * static_cast<int64_t>(sizeof(int32_t));
+    for (Tensor *t : {e->tokens, e->pos}) {
+        t->dims = {n, 1, 1, 1};
+        t->strides = {static_cast<int64_t>(sizeof(int32_t)), bytes, bytes, bytes};
+    }
+    e->tokens->data = e->ids.data();
+    e->pos->data = e->positions.data();
+    int32_t token = -3;
+    {
+        auto graph = e->model->build_graph(*e->ctx);
+        if (!graph) goto fail;
+        if (!graph->compute()) goto fail;
+        if (!e->scheduler->execute(*graph)) goto fail;
+        auto logits = read_logits(*graph->outputs().front(), static_cast<size_t>(n - 1));
+        if (!logits) goto fail;
+        if (last_logits) std::memcpy(last_logits, logits->data(), sizeof(float) * logits->size());
+        e->n_vocab = static_cast<int64_t>(logits->size());
+        Sampler s;
+        auto tok = s.sample(*logits);
+        token = tok ? *tok : -4;
+    }
+    if (!e->ctx->release_kv_access()) return -5;
+    if (!e->cache->commit_append(e->seq)) return -6;
+    return token;
+fail:
+    (void)e->ctx->release_kv_access();
+    (void)e->cache->abort_append(e->seq);
+    return -3;
+}
+
+}  // extern "C"
