@@ -145,7 +145,11 @@ def run_b200(args):
     eng = B.Engine(cfg, kv_capacity=cap, max_batch=PROMPT_LEN, device=local,
                    tp_rank=rank if tp else 0, tp_world=world if tp else 1)
     if args.model == "0.6b":
-        path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", f"/tmp/b200_models_{local}"))
+        if world > 1 and local != 0:
+            dist.barrier()  # local rank 0 writes the seeded GGUF once per box
+        path = G.cached_model(cfg, SEED)
+        if world > 1 and local == 0:
+            dist.barrier()
         eng.load_gguf(path)
     else:
         eng.init_random(SEED)
@@ -271,7 +275,7 @@ def cpu_baseline(cfg, threads=0, sample_steps=16):
     if not oracle.Ref.available():
         return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
     ref = oracle.Ref()
-    path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", "/tmp/b200_models_0"))
+    path = G.cached_model(cfg, SEED)
     eng = oracle.RefEngine(ref, path, threads=threads, capacity=PROMPT_LEN + sample_steps + 1)
     t0 = time.perf_counter()
     tok = eng.eval(prompt_ids(cfg))
@@ -302,7 +306,7 @@ def run_reference(args):
         return
     threads = args.cpu_threads or (os.cpu_count() or 1)
     ref = oracle.Ref()
-    path = G.cached_model(cfg, SEED, os.environ.get("B200_MODEL_DIR", "/tmp/b200_models_0"))
+    path = G.cached_model(cfg, SEED)
     steps, warm = args.steps, args.warmup
     eng = oracle.RefEngine(ref, path, threads=threads, capacity=PROMPT_LEN + steps + warm + 8)
     tok = eng.eval(prompt_ids(cfg))

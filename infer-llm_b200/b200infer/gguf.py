@@ -254,7 +254,7 @@ class GGUFReader:
 
 def cached_model(cfg: Qwen3Config, seed: int, directory: str | None = None) -> str:
     """Path of the seeded GGUF for (cfg, seed), writing it once if absent."""
-    directory = directory or os.environ.get("B200_MODEL_DIR", "/tmp")
+    directory = directory or os.environ.get("B200_MODEL_DIR", "/tmp/b200_models")
     os.makedirs(directory, exist_ok=True)
     key = zlib.crc32(repr(sorted(cfg.as_dict().items())).encode())
     path = os.path.join(directory, f"b200_qwen3_{cfg.n_layer}L{cfg.n_embd}_{key:08x}_s{seed}.gguf")

@@ -51,8 +51,9 @@ int b200_device_supported(int device) {
 
 int b200_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
                  int precision, void *stream) {
-    if (K <= 0 || N <= 0 || M < 0 || !w || !x || !out) return B200_ERR_INVALID_ARGUMENT;
+    if (K <= 0 || N <= 0 || M < 0) return B200_ERR_INVALID_ARGUMENT;
     if (M == 0) return B200_OK;
+    if (!w || !x || !out) return B200_ERR_INVALID_ARGUMENT;
     if (precision != B200_PREC_FFMA && precision != B200_PREC_TF32) return B200_ERR_INVALID_ARGUMENT;
     if ((K & 3) || !aligned16(w) || !aligned16(x)) return B200_ERR_NOT_SUPPORTED;
     if (M <= 4) {

@@ -47,7 +47,7 @@ def test_tiny_matches_reference_golden(cuda, golden, tiny):
 
 def test_graph_decode_equals_stepwise(cuda, tiny):
     cfg = G.QWEN3_TINY
-    eng = B.Engine(cfg, kv_capacity=128, max_batch=16).load_gguf(tiny).finalize()
+    eng = B.Engine(cfg, kv_capacity=128, max_batch=32).load_gguf(tiny).finalize()
     prompt = np.arange(20, dtype=np.int32) * 13 % cfg.n_vocab
     t0 = eng.eval(prompt)
     stepwise = [t0]
