@@ -240,7 +240,7 @@ def run_b200(args):
                    "l2": "inputs larger than L2 (2.38 GB of weights streamed per step)"},
         "ttft_ms": round(float(np.median(ttft)), 3),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        "gpu_launches": steps * (6 * cfg.n_layer + 1) if not tp else None,
+        "gpu_launches": steps * (5 * cfg.n_layer + 1) if not tp else None,
         "clocks": clk.summary(),
     }
     if ops:
@@ -336,8 +336,73 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_op(args):
+    """Op-level timing through the C ABI (BASELINE configs[1] / configs[2] shapes).
+
+    --op gemv|gemm: y = x.W^T with W (N, K) ~ N(0, 0.02), x (M, K) ~ N(0, 1);
+    --op attn: GQA attention (16 q / 8 kv heads, d 128), decode (--M 1, --L cache
+    length) or prefill (--M tokens, causal). Each launch is timed with CUDA events on
+    the launching stream; between launches a 256 MB buffer is overwritten so the
+    next launch starts with a cold L2. Prints one JSON line per shape.
+    """
+    import torch
+    import b200infer as B
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    hbm, peak_kind = peaks()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    st = torch.cuda.current_stream()
+    res = {"op": args.op, "K": args.K, "N": args.N, "M": args.M, "L": args.L}
+    if args.op in ("gemv", "gemm"):
+        w = torch.randn((args.N, args.K), device=dev, generator=g) * 0.02
+        x = torch.randn((args.M, args.K), device=dev, generator=g)
+        out = torch.empty((args.M, args.N), device=dev)
+        fn = lambda: B.mul_mat(w, x, precision=args.precision, out=out)
+        nbytes = 4 * (args.N * args.K + args.M * args.K + args.M * args.N)
+        flops = 2 * args.M * args.N * args.K
+    else:
+        Hq, Hkv, D = 16, 8, 128
+        L = args.L if args.M == 1 else args.M
+        n_past = L - args.M
+        q = torch.randn((args.M, Hq, D), device=dev, generator=g)
+        k = torch.randn((L, Hkv, D), device=dev, generator=g)
+        v = torch.randn((L, Hkv, D), device=dev, generator=g)
+        out = torch.empty_like(q)
+        ws = torch.empty(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, args.M, L), dtype=torch.uint8,
+                         device=dev)
+        fn = lambda: B.flash_attn(q, k, v, n_past, out=out, workspace=ws)
+        nbytes = 4 * (2 * L * Hkv * D + 2 * args.M * Hq * D)
+        causal_pairs = args.M * n_past + args.M * (args.M + 1) / 2
+        flops = 4 * Hq * D * causal_pairs
+    for _ in range(args.warmup):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    us = float(np.median(times))
+    res.update({"us_median": round(us, 3), "us_min": round(min(times), 3),
+                "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "tflops": round(flops / (us * 1e-6) / 1e12, 3),
+                "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4), "peak_kind": peak_kind,
+                "l2": "flushed between launches"})
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", choices=["gemv", "gemm", "attn"], default=None,
+                    help="op-level timing instead of the end-to-end decode benchmark")
+    ap.add_argument("--K", type=int, default=1024)
+    ap.add_argument("--N", type=int, default=1024)
+    ap.add_argument("--M", type=int, default=1)
+    ap.add_argument("--L", type=int, default=1024)
+    ap.add_argument("--precision", type=int, default=0)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
@@ -349,7 +414,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.op:
+        run_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -7,6 +7,7 @@
 // softmax over the visible keys, out = sum p_j v_j. The softmax here is the
 // online (flash) form: same math, different rounding order.
 #include "attention.cuh"
+#include "rope.cuh"
 
 namespace b200 {
 namespace {
@@ -57,7 +58,32 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
     const int ntiles = static_cast<int>((j1 - j0 + kDecTile - 1) / kDecTile);
     const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(D));
 
-    for (int i = tid; i < G * D; i += kDecThreads) qs[i] = a.q[(kvh * G) * D + i];
+    if (a.qkv) {
+        // Fused QK-norm + RoPE (+ KV append in the split that holds position n_past).
+        if (n_past >= a.n_ctx) {
+            if (tid == 0) set_status(a.status, B200_DEV_BAD_POSITION);
+            return;
+        }
+        const bool last = (s == S - 1);
+        const int jobs = G + (last ? 2 : 0);
+        for (int h = warp; h < jobs; h += kDecThreads / 32) {
+            if (h < G) {
+                warp_norm_rope_head<D / 32>(a.qkv + (kvh * G + h) * D, a.q_gamma, a.freq, n_past, a.eps,
+                                            qs + h * D);
+            } else if (h == G) {
+                float *kdst = const_cast<float *>(a.k) + n_past * a.k_tok + kvh * a.k_head;
+                warp_norm_rope_head<D / 32>(a.qkv + (a.Hq + kvh) * D, a.k_gamma, a.freq, n_past, a.eps, kdst);
+            } else {
+                const float *vsrc = a.qkv + (a.Hq + a.Hkv + kvh) * D;
+                float *vdst = const_cast<float *>(a.v) + n_past * a.v_tok + kvh * a.v_head;
+                for (int d = lane; d < D; d += 32) vdst[d] = vsrc[d];
+            }
+        }
+        if (last) __threadfence();  // the appended row is read back below through L2
+    } else {
+        for (int i = tid; i < G * D; i += kDecThreads) qs[i] = a.q[(kvh * G) * D + i];
+    }
+    __syncthreads();
 
     const float *kb = a.k + kvh * a.k_head;
     const float *vb = a.v + kvh * a.v_head;

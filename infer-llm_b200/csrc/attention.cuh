@@ -18,6 +18,15 @@ struct AttnArgs {
     void *ws = nullptr;                  // decode split partials + counters
     size_t ws_bytes = 0;
     int32_t *status = nullptr;
+    // Fused decode prologue (Tq == 1): when qkv is set, q/k/v of the new token are
+    // read raw from the QKV projection [Hq*D | Hkv*D | Hkv*D]; every CTA applies the
+    // per-head RMSNorm + RoPE to its q heads, and the CTA whose split holds position
+    // n_past also normalises/rotates k and appends k and v to the cache (k, v must
+    // then be writable cache pointers).
+    const float *qkv = nullptr;
+    const float *q_gamma = nullptr, *k_gamma = nullptr, *freq = nullptr;
+    float eps = 0.f;
+    int64_t n_ctx = 0;                   // positions >= n_ctx are rejected (status)
 };
 
 // Decode (Tq == 1): fixed `splits` x Hkv CTAs, each a slice of [0, n_past+1),

@@ -165,9 +165,18 @@ B200_DEVICE float rms_scale_from_sumsq(double sumsq, int64_t D, float eps) {
 }  // namespace b200
 
 // Host-side launch helper: launch with the PDL attribute on `stream`.
+// Every kernel asks for the maximum shared-memory carveout, so consecutive kernels
+// never need an SM reconfiguration (which would serialise programmatic launches).
 template <typename Kernel, typename... Args>
 static inline cudaError_t b200_launch(Kernel kernel, dim3 grid, dim3 block, size_t smem,
                                       cudaStream_t stream, bool pdl, Args... args) {
+    static bool carveout_set = false;  // one instance per kernel type
+    if (!carveout_set) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+        carveout_set = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

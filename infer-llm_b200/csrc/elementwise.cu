@@ -7,6 +7,7 @@
 // (graph.cpp:119-131); products that the reference rounds separately are kept
 // unfused (__fmul_rn) so only sin/cos differ (CUDA sincosf vs glibc, <= 1-2 ulp).
 #include "elementwise.cuh"
+#include "rope.cuh"
 
 namespace b200 {
 namespace {
@@ -98,38 +99,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkNormRopeArgs 
     const int64_t hh = is_q ? h : h - a.Hq;
     const float *src = is_q ? a.q_in + t * a.q_ld + hh * D : a.k_in + t * a.k_ld + hh * D;
     float *dst = is_q ? a.q_out + (t * a.Hq + hh) * D : a.k_out + row * a.k_out_ld + hh * D;
-    const float *gamma = is_q ? a.q_gamma : a.k_gamma;
-
-    float v[E];
-    double ss = 0.0;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        v[e] = src[lane * E + e];
-        const float sq = v[e] * v[e];
-        ss += static_cast<double>(sq);
-    }
-    ss = warp_sum(ss);
-    const float sc = rms_scale_from_sumsq(ss, D, a.eps);
-#pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc), gamma[lane * E + e]);
-
-    const bool lo = lane < 16;
-    const int64_t half = D / 2;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-        const int64_t j = (lo ? lane : lane - 16) * E + e;  // pair index < D/2
-        const float ang = static_cast<float>(static_cast<double>(p) * static_cast<double>(a.freq[j]));
-        float s, c;
-        sincosf(ang, &s, &c);
-        float r;
-        if (lo)  // x0 = v, x1 = other
-            r = __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s));
-        else     // x0 = other, x1 = v
-            r = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
-        dst[lane * E + e] = r;
-    }
-    (void)half;
+    warp_norm_rope_head<E>(src, is_q ? a.q_gamma : a.k_gamma, a.freq, p, a.eps, dst);
 }
 
 // ---------------------------------------------------------------------------

@@ -213,7 +213,8 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         r.n_ctx = e->c.kv_capacity;
         r.eps = e->c.rms_eps;
         r.status = e->status;
-        B200_TRY(mark(e, "qk_norm_rope_kv", qk_norm_rope_launch(r, st, pdl)));
+        // single-token decode: the attention kernel applies QK-norm + RoPE and appends K/V itself
+        if (M > 1) B200_TRY(mark(e, "qk_norm_rope_kv", qk_norm_rope_launch(r, st, pdl)));
 
         AttnArgs a;
         a.q = e->q;
@@ -232,6 +233,12 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         a.ws = e->attn_ws;
         a.ws_bytes = e->attn_ws_bytes;
         a.status = e->status;
+        a.qkv = e->qkv;
+        a.q_gamma = w.q_norm;
+        a.k_gamma = w.k_norm;
+        a.freq = e->freq;
+        a.eps = e->c.rms_eps;
+        a.n_ctx = e->c.kv_capacity;
         if (M == 1)
             B200_TRY(mark(e, "attn_decode", attn_decode_launch(a, e->attn_splits, st, pdl)));
         else

@@ -21,7 +21,7 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kMaxRpc = 8;
 constexpr uint32_t kStageTarget = 16384;   // bytes per stage (rows are kept whole)
-constexpr uint32_t kStageBudget = 65536;   // ring size target
+constexpr uint32_t kStageBudget = 98304;   // ring size target
 
 struct Layout {
     int rpc;          // weight rows per stage
@@ -31,7 +31,7 @@ struct Layout {
     size_t off_x, off_stage, off_part, off_best;
 };
 
-Layout make_layout(int64_t K, int M, int epi) {
+Layout make_layout(int64_t K, int M, int epi, int64_t rows_cta) {
     Layout L;
     const uint32_t row_bytes = static_cast<uint32_t>(K * 4);
     int rpc = static_cast<int>(std::max<uint32_t>(1u, kStageTarget / row_bytes));
@@ -50,7 +50,8 @@ Layout make_layout(int64_t K, int M, int epi) {
     L.off_stage = off;
     off += static_cast<size_t>(L.stages) * stage_bytes;
     L.off_part = off;
-    off += 2 * kConsumerWarps * kMaxRpc * 4 * sizeof(float);  // [2][slice][row][m]
+    off += static_cast<size_t>(rows_cta) * (kConsumerWarps / rpc) * M * sizeof(float);  // [row][slice][m]
+    off = (off + 15) & ~size_t(15);
     L.off_best = off;
     off += 64;
     L.smem = off;
@@ -174,149 +175,158 @@ gemv_kernel(const GemvArgs a, const int rpc, const int stages, const uint32_t st
     const int64_t K4 = K >> 2;
     const int64_t L4 = (K4 + ks - 1) / ks;
     const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    float best_v = -INFINITY;
-    int32_t best_i = -1;
-    bool bad = false;
+    const int item_r = warp % rpc, item_sl = warp / rpc;  // this warp's (row, K-slice) in every stage
 
+    // Main loop: warps are coupled only through the stage mbarriers. Each warp
+    // reduces its (row, K-slice) dot product with shuffles and parks it in
+    // part[local_row][slice][m]; the slices are combined once, after the loop.
     for (int c = 0; c < n_chunks; ++c) {
         const int s = c % stages;
-        // A wait that gives up is made collective: the warp still reaches the
-        // named barrier below and every consumer leaves after it together.
-        const bool landed = mbar_wait(&full[s], (c / stages) & 1);
-        if (!landed) {
+        if (!mbar_wait(&full[s], (c / stages) & 1)) {  // bounded: never a hang
             set_status(a.status, B200_DEV_TIMEOUT);
             s_abort = 1;
+            break;
         }
         const int64_t row0 = r0 + static_cast<int64_t>(c) * rpc;
-        const int rows = landed ? static_cast<int>(min64(rpc, r1 - row0)) : 0;
+        const int rows = static_cast<int>(min64(rpc, r1 - row0));
         const float4 *st4 = reinterpret_cast<const float4 *>(stage + static_cast<size_t>(s) * stage_floats);
-        float *pb = part + (c & 1) * (kConsumerWarps * kMaxRpc * 4);
-        {
-            const int item = warp;          // one item per warp: rpc * ks == 8
-            const int r = item % rpc, sl = item / rpc;
+        if (item_r < rows) {
             float acc[M];
 #pragma unroll
             for (int m = 0; m < M; ++m) acc[m] = 0.f;
-            if (r < rows) {
-                const int64_t beg = sl * L4, end = min64(K4, beg + L4);
-                const float4 *wr = st4 + r * K4;
+            const int64_t beg = item_sl * L4, end = min64(K4, beg + L4);
+            const float4 *wr = st4 + item_r * K4;
 #pragma unroll 4
-                for (int64_t i = beg + lane; i < end; i += 32) {
-                    const float4 wv = wr[i];
+            for (int64_t i = beg + lane; i < end; i += 32) {
+                const float4 wv = wr[i];
 #pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        const float4 xv = xs4[m * K4 + i];
-                        acc[m] = fmaf(wv.x, xv.x, acc[m]);
-                        acc[m] = fmaf(wv.y, xv.y, acc[m]);
-                        acc[m] = fmaf(wv.z, xv.z, acc[m]);
-                        acc[m] = fmaf(wv.w, xv.w, acc[m]);
-                    }
+                for (int m = 0; m < M; ++m) {
+                    const float4 xv = xs4[m * K4 + i];
+                    acc[m] = fmaf(wv.x, xv.x, acc[m]);
+                    acc[m] = fmaf(wv.y, xv.y, acc[m]);
+                    acc[m] = fmaf(wv.z, xv.z, acc[m]);
+                    acc[m] = fmaf(wv.w, xv.w, acc[m]);
                 }
             }
+            const int64_t lr = row0 - r0 + item_r;
 #pragma unroll
             for (int m = 0; m < M; ++m) {
                 const float v = warp_sum(acc[m]);
-                if (lane == 0) pb[(sl * kMaxRpc + r) * 4 + m] = v;
+                if (lane == 0) part[(lr * ks + item_sl) * M + m] = v;
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        named_sync(1, kConsumers);
-        if (*(volatile int *)&s_abort) break;
+    }
+    named_sync(1, kConsumers);  // every partial is in shared memory
+    const bool aborted = *(volatile int *)&s_abort != 0;
+    const int rows_cta = static_cast<int>(r1 - r0);
 
-        // Combine the K-slices of each (row, token) in a fixed order + epilogue.
-        if (EPI == GEMV_SWIGLU) {
-            const int pairs = rows / 2;
-            if (tid < pairs * M) {
-                const int p = tid / M, m = tid % M;
-                float g = 0.f, u = 0.f;
-                for (int sl = 0; sl < ks; ++sl) {
-                    g += pb[(sl * kMaxRpc + 2 * p) * 4 + m];
-                    u += pb[(sl * kMaxRpc + 2 * p + 1) * 4 + m];
-                }
-                const int64_t o_ld = a.out_ld ? a.out_ld : a.N / 2;
-                const float sg = g / (1.0f + expf(-g));
-                a.out[m * o_ld + (row0 / 2 + p)] = u * sg;
+    // Combine the K-slices of every (row, token) in slice order, then the epilogue.
+    if (EPI == GEMV_SWIGLU) {
+        const int64_t o_ld = a.out_ld ? a.out_ld : a.N / 2;
+        for (int t = tid; t < (rows_cta / 2) * M && !aborted; t += kConsumers) {
+            const int p = t / M, m = t % M;
+            float g = 0.f, u = 0.f;
+            for (int sl = 0; sl < ks; ++sl) {
+                g += part[((2 * p) * ks + sl) * M + m];
+                u += part[((2 * p + 1) * ks + sl) * M + m];
             }
-        } else if (EPI == GEMV_ARGMAX) {
-            // M == 1: warp 0 reduces the chunk's rows in order.
-            if (warp == 0) {
-                float v = -INFINITY;
-                if (lane < rows) {
-                    v = 0.f;
-                    for (int sl = 0; sl < ks; ++sl) v += pb[(sl * kMaxRpc + lane) * 4];
-                    if (a.out) a.out[row0 + lane] = v;
-                    if (isnan(v) || v == INFINITY) bad = true;
-                }
-                // first maximum of the chunk (lowest row on ties)
-                float bv = v;
-                int bi = (lane < rows) ? lane : 0x7fffffff;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > bv || (ov == bv && oi < bi)) {
-                        bv = ov;
-                        bi = oi;
-                    }
-                }
-                bad = __any_sync(0xffffffffu, bad);
-                if (bv > best_v && bi != 0x7fffffff) {
-                    best_v = bv;
-                    best_i = static_cast<int32_t>(row0 + bi);
-                }
-            }
-        } else {
-            if (tid < rows * M) {
-                const int r = tid / M, m = tid % M;
-                float v = 0.f;
-                for (int sl = 0; sl < ks; ++sl) v += pb[(sl * kMaxRpc + r) * 4 + m];
-                const int64_t o_ld = a.out_ld ? a.out_ld : a.N;
-                const int64_t idx = m * o_ld + row0 + r;
-                if (EPI == GEMV_RESIDUAL) v = v + a.residual[idx];
-                a.out[idx] = v;
+            const float sg = g / (1.0f + expf(-g));
+            a.out[m * o_ld + (r0 / 2 + p)] = u * sg;
+        }
+    } else if (EPI == GEMV_ARGMAX) {
+        // M == 1. Per thread: rows tid, tid+256, ... (increasing), strict '>' keeps
+        // the first maximum; then a block reduction that prefers the lower row on ties.
+        float bv = -INFINITY;
+        int64_t bi = INT64_MAX;
+        bool bad = aborted;
+        for (int r = tid; r < rows_cta && !aborted; r += kConsumers) {
+            float v = 0.f;
+            for (int sl = 0; sl < ks; ++sl) v += part[r * ks + sl];
+            if (a.out) a.out[r0 + r] = v;
+            if (isnan(v) || v == INFINITY) bad = true;
+            if (v > bv) {
+                bv = v;
+                bi = r0 + r;
             }
         }
-    }
-
-    if (EPI == GEMV_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        bad = __any_sync(0xffffffffu, bad);
+        __shared__ float s_bv[kConsumerWarps];
+        __shared__ int64_t s_bi[kConsumerWarps];
+        __shared__ int s_bad[kConsumerWarps];
         __shared__ unsigned s_ticket;
+        if (lane == 0) {
+            s_bv[warp] = bv;
+            s_bi[warp] = bi;
+            s_bad[warp] = bad;
+        }
+        named_sync(1, kConsumers);
         if (tid == 0) {
-            a.part_val[blockIdx.x] = bad ? NAN : best_v;
-            a.part_idx[blockIdx.x] = bad ? -2 : best_i;
+            float v = s_bv[0];
+            int64_t i = s_bi[0];
+            bool anyb = s_bad[0];
+            for (int w = 1; w < kConsumerWarps; ++w) {
+                anyb |= s_bad[w] != 0;
+                if (s_bv[w] > v || (s_bv[w] == v && s_bi[w] < i)) {
+                    v = s_bv[w];
+                    i = s_bi[w];
+                }
+            }
+            a.part_val[blockIdx.x] = anyb ? NAN : v;
+            a.part_idx[blockIdx.x] = anyb ? -2 : (i == INT64_MAX ? -1 : static_cast<int32_t>(i));
             __threadfence();
             s_ticket = atomicAdd(a.counter, 1u);
         }
         named_sync(1, kConsumers);
         if (s_ticket == static_cast<unsigned>(G - 1) && tid == 0) {
             __threadfence();
-            float bv = -INFINITY;
-            int32_t bi = -1;
+            float gv = -INFINITY;
+            int32_t gi = -1;
             bool any_bad = false;
             for (int b = 0; b < G; ++b) {  // CTAs own increasing row ranges
                 const float v = __ldcg(a.part_val + b);
                 const int32_t i = __ldcg(a.part_idx + b);
                 if (i == -2) any_bad = true;
-                if (v > bv) {
-                    bv = v;
-                    bi = i;
+                if (v > gv) {
+                    gv = v;
+                    gi = i;
                 }
             }
-            if (any_bad || bi < 0) {
-                bi = -1;
+            if (any_bad || gi < 0) {
+                gi = -1;
                 set_status(a.status, B200_DEV_BAD_LOGITS);
             } else {
-                bi = static_cast<int32_t>(bi + a.idx_offset);
+                gi = static_cast<int32_t>(gi + a.idx_offset);
             }
-            *a.argmax_out = bi;
-            if (a.best_val_out) *a.best_val_out = any_bad ? NAN : bv;
+            *a.argmax_out = gi;
+            if (a.best_val_out) *a.best_val_out = any_bad ? NAN : gv;
             if (a.token_log) {
                 const int32_t p = *a.log_pos;
-                a.token_log[p % a.log_cap] = bi;
+                a.token_log[p % a.log_cap] = gi;
                 *a.log_pos = p + 1;
             }
             if (a.n_past) *a.n_past += a.n_past_add;
             *a.counter = 0u;
+        }
+    } else {
+        const int64_t o_ld = a.out_ld ? a.out_ld : a.N;
+        for (int t = tid; t < rows_cta * M && !aborted; t += kConsumers) {
+            const int r = t / M, m = t % M;
+            float v = 0.f;
+            for (int sl = 0; sl < ks; ++sl) v += part[(r * ks + sl) * M + m];
+            const int64_t idx = m * o_ld + r0 + r;
+            if (EPI == GEMV_RESIDUAL) v = v + a.residual[idx];
+            a.out[idx] = v;
         }
     }
 }
@@ -369,9 +379,11 @@ cudaError_t gemv_launch(const GemvArgs &a, cudaStream_t stream, bool pdl) {
     if (a.M < 1 || a.M > 4 || (a.K & 3) || a.K <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == GEMV_ARGMAX && a.M != 1) return cudaErrorInvalidValue;
     if (a.epi == GEMV_SWIGLU && (a.N & 1)) return cudaErrorInvalidValue;
-    const Layout L = make_layout(a.K, a.M, a.epi);
-    if (L.smem > 200 * 1024) return cudaErrorInvalidValue;
     const int grid = gemv_grid_size(a.N, a.epi);
+    const int unit = (a.epi == GEMV_SWIGLU) ? 2 : 1;
+    const int64_t rows_cta = ((a.N / unit + grid - 1) / grid) * unit;
+    const Layout L = make_layout(a.K, a.M, a.epi, rows_cta);
+    if (L.smem > 200 * 1024) return cudaErrorInvalidValue;
     switch (a.M) {
         case 1: return launch_m<1>(a, L, grid, stream, pdl);
         case 2: return launch_m<2>(a, L, grid, stream, pdl);
