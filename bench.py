@@ -127,6 +127,34 @@ def gemv_bytes(cfg):
             "lm_head_gemv": 4 * cfg.n_vocab * H}
 
 
+def trace_summary(tr, cfg):
+    """Per kernel class of one graph-replayed step: mean span (first CTA start to last
+    CTA end), mean gap from the previous launch's end to this launch's first CTA start
+    (negative = overlap under programmatic launch), mean wait of CTA 0 for its
+    predecessor, and the step's total span."""
+    names = []
+    for _ in range(cfg.n_layer):
+        names += ["qkv_gemv", "attn_decode", "o_proj_gemv", "gate_up_gemv", "down_gemv"]
+    names.append("lm_head_gemv")
+    tr = tr.astype(np.int64)
+    out = {}
+    for i, nm in enumerate(names[:len(tr)]):
+        span = (tr[i, 2] - tr[i, 3]) / 1e3
+        gap = (tr[i, 3] - tr[i - 1, 2]) / 1e3 if i else 0.0
+        wait = (tr[i, 1] - tr[i, 0]) / 1e3
+        resolve = (tr[i, 1] - tr[i - 1, 2]) / 1e3 if i else 0.0  # predecessor end -> wait returns
+        prologue = (tr[i, 4] - tr[i, 1]) / 1e3 if tr[i, 4] else 0.0
+        main = (tr[i, 5] - tr[i, 4]) / 1e3 if tr[i, 5] else 0.0
+        tail = (tr[i, 2] - tr[i, 5]) / 1e3 if tr[i, 5] else 0.0  # CTA0 main loop end -> last CTA end
+        d = out.setdefault(nm, [0] + [0.0] * 7)
+        for j, v in enumerate((1, span, gap, wait, resolve, prologue, main, tail)):
+            d[j] += v
+    keys = ("span_us", "gap_us", "wait_us", "resolve_us", "prologue_us", "main_us", "tail_us")
+    res = {nm: {k: round(v[j + 1] / v[0], 2) for j, k in enumerate(keys)} for nm, v in out.items()}
+    res["step_us"] = round((tr[len(names[:len(tr)]) - 1, 2] - tr[0, 3]) / 1e3, 1)
+    return res
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -226,6 +254,9 @@ def run_b200(args):
             for i in range(n):
                 nm = names.raw[i * 32:(i + 1) * 32].split(b"\0")[0].decode()
                 ops[nm] = ops.get(nm, 0.0) + us[i] / reps
+    trace = {}
+    if not tp:
+        trace = trace_summary(eng.trace(), cfg)
     hbm, peak_kind = peaks()
     ctx_mid = PROMPT_LEN + steps // 2
     res = {
@@ -255,6 +286,8 @@ def run_b200(args):
         res["step_roofline"] = {"achieved": round(step_gbs, 1), "frac": round(step_gbs / hbm, 4),
                                 "bytes_per_step": step_bytes(cfg, ctx_mid)}
         res["ops_us_per_step_eager"] = {k: round(v, 2) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
+    if trace:
+        res["graph_trace"] = trace
     if rank == 0 and world == 1 and args.model == "0.6b" and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_threads, sample_steps=args.cpu_sample_steps)
     res["first_tokens"] = [int(first)] + [int(t) for t in toks[:8]]

@@ -205,6 +205,15 @@ int b200_engine_generate(b200_engine *e, int64_t n_steps, int32_t *host_tokens);
 int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *us,
                              int max_ops);
 
+/* Device-side timeline of one graph-replayed decode step: for each launch, in
+ * order (per layer: QKV GEMV, attention, o_proj, gate/up, down; then LM head),
+ * 8 global-timer words in ns: [CTA 0 start, CTA 0 after its dependency wait,
+ * last CTA end, first CTA start of any CTA, CTA 0 after its prologue, CTA 0
+ * after its main loop, 0, 0]. Returns the
+ * number of launches written (<= max_kernels) or < 0. The step leaves n_past
+ * and the token unchanged. */
+int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int max_kernels);
+
 /* Raw handles for in-process callers (bench / tests): the engine's stream and
  * device status word. */
 void *b200_engine_stream(b200_engine *e);

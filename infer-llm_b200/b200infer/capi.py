@@ -68,6 +68,7 @@ _SIGS = {
     "b200_engine_eval": ([_vp, _vp, _i64, _vp, _vp], C.c_int),
     "b200_engine_generate": ([_vp, _i64, _vp], C.c_int),
     "b200_engine_profile_step": ([_vp, _vp, C.c_int, _vp, C.c_int], C.c_int),
+    "b200_engine_trace_step": ([_vp, _vp, C.c_int], C.c_int),
     "b200_engine_stream": ([_vp], _vp),
     "b200_engine_read_status": ([_vp, _vp], C.c_int),
     "b200_tp_unique_id": ([_vp], C.c_int),

@@ -106,6 +106,17 @@ class Engine:
         _chk("b200_engine_generate", lib().b200_engine_generate(self.h, n_steps, C.c_void_p(out.ctypes.data)))
         return out[:n_steps]
 
+    def trace(self) -> np.ndarray:
+        """Device timeline of one graph-replayed decode step: (launches, 8) ns stamps
+        [CTA0 start, CTA0 after dependency wait, last CTA end, first CTA start,
+        CTA0 after prologue, CTA0 after main loop, -, -]."""
+        cap = 5 * self.cfg.n_layer + 8
+        buf = np.zeros((cap, 8), np.uint64)
+        n = lib().b200_engine_trace_step(self.h, C.c_void_p(buf.ctypes.data), cap)
+        if n < 0:
+            raise B200Error("b200_engine_trace_step", -n)
+        return buf[:n]
+
     def stream(self) -> int:
         return int(lib().b200_engine_stream(self.h) or 0)
 

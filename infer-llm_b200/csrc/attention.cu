@@ -21,7 +21,7 @@ struct DecWs {
     float *o;            // [Hkv][S][G][D]
 };
 
-__host__ __device__ inline DecWs dec_ws(void *base, int64_t D, int64_t Hq, int64_t Hkv, int S) {
+__host__ __device__ inline DecWs dec_ws(void *base, int64_t Hq, int64_t Hkv, int S) {
     DecWs w;
     unsigned char *p = static_cast<unsigned char *>(base);
     w.counters = reinterpret_cast<unsigned *>(p);
@@ -30,10 +30,18 @@ __host__ __device__ inline DecWs dec_ws(void *base, int64_t D, int64_t Hq, int64
     off += static_cast<size_t>(Hq) * S * 2 * 4;
     off = (off + 255) & ~size_t(255);
     w.o = reinterpret_cast<float *>(p + off);
-    (void)D;
     return w;
 }
 
+// Split-KV flash decoding for one query token. CTA (s, kvh) covers keys
+// [L*s/S, L*(s+1)/S) of KV head kvh for its G query heads, in 32-key tiles
+// (double-buffered cp.async), with an online softmax; the last CTA of each KV
+// head to finish merges the S partial (m, l, o) triples in split order.
+//
+// Fused prologue (a.qkv set): q/k come raw from the QKV projection; the CTA
+// applies the per-head RMSNorm + RoPE to its q heads and the CTA holding
+// position n_past also normalises/rotates k, appends k and v to the cache and
+// patches that row into its shared-memory tile directly.
 template <int D, int G>
 __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs a, const int S) {
     constexpr int LD = D + 4;
@@ -42,48 +50,30 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
     float *Ks = sm;                            // [2][32][LD]
     float *Vs = Ks + 2 * kDecTile * LD;        // [2][32][LD]
     float *qs = Vs + 2 * kDecTile * LD;        // [G][D]
-    float *P = qs + G * D;                     // [G][32]
+    float *knew = qs + G * D;                  // [D] new token's k (normed, rotated)
+    float *vnew = knew + D;                    // [D] new token's v
+    float *P = vnew + D;                       // [G][32]
     float *alpha_s = P + G * kDecTile;         // [G]
     __shared__ unsigned s_ticket;
 
+    const TraceMark tm(a.trace);
     grid_launch_dependents();
-    grid_wait();
-
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x;
     const int64_t kvh = blockIdx.y;
+    const bool fused = a.qkv != nullptr;
+
+    // n_past is final before this kernel starts when early_kv is set (see attention.cuh)
+    if (!a.early_kv) grid_wait();
     const int64_t n_past = a.n_past_dev ? static_cast<int64_t>(*a.n_past_dev) : a.n_past;
-    const int64_t L = n_past + 1;  // Tq == 1: keys 0..n_past are visible
+    const int64_t L = n_past + 1;  // keys 0..n_past are visible to the single query
     const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
+    const bool last = (s == S - 1);  // holds key n_past
     const int ntiles = static_cast<int>((j1 - j0 + kDecTile - 1) / kDecTile);
     const float scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(D));
-
-    if (a.qkv) {
-        // Fused QK-norm + RoPE (+ KV append in the split that holds position n_past).
-        if (n_past >= a.n_ctx) {
-            if (tid == 0) set_status(a.status, B200_DEV_BAD_POSITION);
-            return;
-        }
-        const bool last = (s == S - 1);
-        const int jobs = G + (last ? 2 : 0);
-        for (int h = warp; h < jobs; h += kDecThreads / 32) {
-            if (h < G) {
-                warp_norm_rope_head<D / 32>(a.qkv + (kvh * G + h) * D, a.q_gamma, a.freq, n_past, a.eps,
-                                            qs + h * D);
-            } else if (h == G) {
-                float *kdst = const_cast<float *>(a.k) + n_past * a.k_tok + kvh * a.k_head;
-                warp_norm_rope_head<D / 32>(a.qkv + (a.Hq + kvh) * D, a.k_gamma, a.freq, n_past, a.eps, kdst);
-            } else {
-                const float *vsrc = a.qkv + (a.Hq + a.Hkv + kvh) * D;
-                float *vdst = const_cast<float *>(a.v) + n_past * a.v_tok + kvh * a.v_head;
-                for (int d = lane; d < D; d += 32) vdst[d] = vsrc[d];
-            }
-        }
-        if (last) __threadfence();  // the appended row is read back below through L2
-    } else {
-        for (int i = tid; i < G * D; i += kDecThreads) qs[i] = a.q[(kvh * G) * D + i];
-    }
-    __syncthreads();
+    // In fused mode row n_past is produced by this kernel: it is zero-filled by the
+    // tile load and patched from knew / vnew.
+    const int64_t jload = fused ? min64(j1, n_past) : j1;
 
     const float *kb = a.k + kvh * a.k_head;
     const float *vb = a.v + kvh * a.v_head;
@@ -93,13 +83,50 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
         for (int i = tid; i < kDecTile * C4; i += kDecThreads) {
             const int r = i / C4, c = i % C4;
             const int64_t j = base + r;
-            const bool ok = j < j1;
-            const int64_t jj = ok ? j : j0;
+            const bool ok = j < jload;
+            const int64_t jj = ok ? j : 0;
             cp_async16_zfill(Ks + (buf * kDecTile + r) * LD + c * 4, kb + jj * a.k_tok + c * 4, ok);
             cp_async16_zfill(Vs + (buf * kDecTile + r) * LD + c * 4, vb + jj * a.v_tok + c * 4, ok);
         }
         cp_async_commit();
     };
+    // cached keys stream in while the previous kernel finishes
+    if (ntiles > 0) load_tile(0, 0);
+    if (ntiles > 1) load_tile(1, 1);
+
+    if (a.early_kv) grid_wait();
+    tm.waited();
+    if (fused) {
+        if (n_past >= a.n_ctx) {
+            if (tid == 0) set_status(a.status, B200_DEV_BAD_POSITION);
+            cp_async_wait<0>();
+            return;
+        }
+        const int jobs = G + (last ? 2 : 0);
+        for (int h = warp; h < jobs; h += kDecThreads / 32) {
+            if (h < G) {
+                warp_norm_rope_head<D / 32>(a.qkv + (kvh * G + h) * D, a.q_gamma, a.freq, n_past, a.eps,
+                                            qs + h * D);
+            } else if (h == G) {
+                warp_norm_rope_head<D / 32>(a.qkv + (a.Hq + kvh) * D, a.k_gamma, a.freq, n_past, a.eps, knew);
+                __syncwarp();
+                float *kdst = const_cast<float *>(a.k) + n_past * a.k_tok + kvh * a.k_head;
+                for (int d = lane; d < D; d += 32) kdst[d] = knew[d];
+            } else {
+                const float *vsrc = a.qkv + (a.Hq + a.Hkv + kvh) * D;
+                float *vdst = const_cast<float *>(a.v) + n_past * a.v_tok + kvh * a.v_head;
+                for (int d = lane; d < D; d += 32) {
+                    const float v = vsrc[d];
+                    vnew[d] = v;
+                    vdst[d] = v;
+                }
+            }
+        }
+    } else {
+        for (int i = tid; i < G * D; i += kDecThreads) qs[i] = a.q[(kvh * G) * D + i];
+    }
+    __syncthreads();
+    tm.at(4);
 
     float m_run = -INFINITY, l_run = 0.f;  // valid in warp g (< G), replicated over lanes
     float acc[G][DPT];
@@ -108,18 +135,22 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
 #pragma unroll
         for (int e = 0; e < DPT; ++e) acc[g][e] = 0.f;
 
-    if (ntiles > 0) load_tile(0, 0);
     for (int t = 0; t < ntiles; ++t) {
         const int buf = t & 1;
-        if (t + 1 < ntiles) {
-            load_tile(t + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        if (t + 1 < ntiles) cp_async_wait<1>();
+        else cp_async_wait<0>();
         __syncthreads();
+        const int64_t tbase = j0 + static_cast<int64_t>(t) * kDecTile;
+        if (fused && last && n_past >= tbase && n_past < tbase + kDecTile) {
+            const int r = static_cast<int>(n_past - tbase);
+            for (int d = tid; d < D; d += kDecThreads) {
+                Ks[(buf * kDecTile + r) * LD + d] = knew[d];
+                Vs[(buf * kDecTile + r) * LD + d] = vnew[d];
+            }
+            __syncthreads();
+        }
         if (warp < G) {
-            const int64_t j = j0 + static_cast<int64_t>(t) * kDecTile + lane;
+            const int64_t j = tbase + lane;
             const bool valid = j < j1;
             const float *kr = Ks + (buf * kDecTile + lane) * LD;
             const float *qr = qs + warp * D;
@@ -158,10 +189,12 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
             }
         }
         __syncthreads();
+        if (t + 2 < ntiles) load_tile(t + 2, buf);
     }
+    tm.at(5);
 
     // partials
-    DecWs w = dec_ws(a.ws, D, a.Hq, a.Hkv, S);
+    DecWs w = dec_ws(a.ws, a.Hq, a.Hkv, S);
     const int64_t slot = (kvh * S + s) * G;
     if (warp < G && lane == 0) {
         w.ml[(slot + warp) * 2 + 0] = m_run;
@@ -178,7 +211,10 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
     __syncthreads();
     if (tid == 0) s_ticket = atomicAdd(w.counters + kvh, 1u);
     __syncthreads();
-    if (s_ticket != static_cast<unsigned>(S - 1)) return;
+    if (s_ticket != static_cast<unsigned>(S - 1)) {
+        tm.done();
+        return;
+    }
     __threadfence();
     // Last CTA of this KV head: merge the S splits in split order.
 #pragma unroll
@@ -202,6 +238,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
         }
     }
     if (tid == 0) w.counters[kvh] = 0u;
+    tm.done();
 }
 
 // ---------------------------------------------------------------------------
@@ -209,6 +246,11 @@ constexpr int kPreThreads = 256;
 constexpr int kRows = 64;   // query rows (token, head) per CTA
 constexpr int kKeys = 64;   // keys per tile
 
+// Prefill / multi-token attention: a CTA owns 64 query rows (BQ = 64/G tokens x
+// the G query heads of one KV head), streams 64-key K and V tiles (cp.async; V
+// loads overlap QK^T, the next K tile overlaps PV) and keeps an online softmax
+// per row. Tiles beyond the causal limit of the block are skipped; the heaviest
+// blocks are scheduled first.
 template <int D, int G>
 __global__ void __launch_bounds__(kPreThreads, 1) attn_prefill_kernel(const AttnArgs a) {
     constexpr int LD = D + 4;
@@ -371,10 +413,14 @@ __global__ void __launch_bounds__(kPreThreads, 1) attn_prefill_kernel(const Attn
 
 template <int D, int G>
 cudaError_t dec_launch(const AttnArgs &a, int S, cudaStream_t stream, bool pdl) {
-    const size_t smem = (4 * kDecTile * (D + 4) + G * D + G * kDecTile + G) * sizeof(float);
+    const size_t smem = (4 * kDecTile * (D + 4) + G * D + 2 * D + G * kDecTile + G) * sizeof(float);
     auto kern = attn_decode_kernel<D, G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
+    static bool configured = false;  // one instance per template instantiation
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
     return b200_launch(kern, dim3(S, static_cast<unsigned>(a.Hkv)), dim3(kDecThreads), smem, stream, pdl, a, S);
 }
 
@@ -383,8 +429,12 @@ cudaError_t pre_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
     constexpr int BQ = kRows / G;
     const size_t smem = ((kRows + 2 * kKeys) * (D + 4) + kRows * (kKeys + 4)) * sizeof(float);
     auto kern = attn_prefill_kernel<D, G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
     const dim3 grid(static_cast<unsigned>((a.Tq + BQ - 1) / BQ), static_cast<unsigned>(a.Hkv));
     return b200_launch(kern, grid, dim3(kPreThreads), smem, stream, pdl, a);
 }
@@ -414,7 +464,7 @@ cudaError_t pre_by_g(const AttnArgs &a, cudaStream_t st, bool pdl) {
 bool strides_ok(const AttnArgs &a) {
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     return a.Hkv > 0 && a.Hq % a.Hkv == 0 && (a.k_tok & 3) == 0 && (a.k_head & 3) == 0 &&
-           (a.v_tok & 3) == 0 && (a.v_head & 3) == 0 && al(a.q) && al(a.k) && al(a.v);
+           (a.v_tok & 3) == 0 && (a.v_head & 3) == 0 && al(a.q ? a.q : a.qkv) && al(a.k) && al(a.v);
 }
 
 }  // namespace

@@ -27,6 +27,11 @@ struct AttnArgs {
     const float *q_gamma = nullptr, *k_gamma = nullptr, *freq = nullptr;
     float eps = 0.f;
     int64_t n_ctx = 0;                   // positions >= n_ctx are rejected (status)
+    unsigned long long *trace = nullptr;  // optional step trace slot (common.cuh)
+    // The launch before this one signals its dependents only after its own wait
+    // (GemvArgs::late_launch): n_past and the cached K/V rows [0, n_past) are then
+    // complete when this kernel starts and are read before its dependency wait.
+    bool early_kv = false;
 };
 
 // Decode (Tq == 1): fixed `splits` x Hkv CTAs, each a slice of [0, n_past+1),

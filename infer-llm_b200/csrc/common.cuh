@@ -27,6 +27,36 @@ B200_DEVICE void set_status(int32_t *status, int32_t code) {
 }
 
 // ---------------------------------------------------------------------------
+// Device-side step trace: a kernel given a trace slot (8 x u64, preset to
+// {0, 0, 0, UINT64_MAX, 0...}) records the global timer at CTA 0's start [0],
+// after CTA 0's dependency wait [1], the last CTA end [2], the first CTA start
+// [3], CTA 0 after its prologue (inputs staged) [4] and after its main loop [5].
+B200_DEVICE uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+struct TraceMark {
+    unsigned long long *slot;
+    B200_DEVICE explicit TraceMark(unsigned long long *s) : slot(s) {
+        if (slot && threadIdx.x == 0) {
+            const unsigned long long t = global_ns();
+            if (blockIdx.x == 0 && blockIdx.y == 0) slot[0] = t;
+            atomicMin(slot + 3, t);
+        }
+    }
+    B200_DEVICE void waited() const {
+        if (slot && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) slot[1] = global_ns();
+    }
+    B200_DEVICE void at(int k) const {
+        if (slot && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) slot[k] = global_ns();
+    }
+    B200_DEVICE void done() const {
+        if (slot && threadIdx.x == 0) atomicMax(slot + 2, static_cast<unsigned long long>(global_ns()));
+    }
+};
+
+// ---------------------------------------------------------------------------
 // Programmatic dependent launch (PDL). Every kernel launched with the
 // programmatic-serialization attribute calls grid_wait() before it reads data
 // produced by the previous kernel in the stream, and grid_launch_dependents()

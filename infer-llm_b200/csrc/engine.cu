@@ -111,6 +111,7 @@ struct b200_engine {
     float *am_val = nullptr;
     int32_t *am_idx = nullptr;
     unsigned *am_counter = nullptr;
+    int am_slots = 0;  // per-CTA argmax partials of the LM head GEMV (+1 local winner slot)
     float *tp_pairs = nullptr;  // [world][2] (value, index) for the vocab-sharded argmax
     // state
     int64_t n_past = 0;
@@ -121,6 +122,10 @@ struct b200_engine {
     bool graph_logits = false;
     b200_tp *tp = nullptr;
     int32_t *pinned_io = nullptr;  // small pinned host buffer for per-step ids / tokens
+    // device-side step trace (b200_engine_trace_step): 8 x u64 per launch
+    unsigned long long *trace_buf = nullptr;
+    int trace_cap = 0, trace_n = 0;
+    bool trace_on = false;
     // per-op timing (b200_engine_profile_step): an event is recorded after each launch
     std::vector<cudaEvent_t> *prof_events = nullptr;
     std::vector<const char *> *prof_names = nullptr;
@@ -136,6 +141,11 @@ inline cudaError_t mark(b200_engine *e, const char *name, cudaError_t launched) 
     e->prof_events->push_back(ev);
     e->prof_names->push_back(name);
     return cudaEventRecord(ev, e->stream);
+}
+
+inline unsigned long long *next_trace(b200_engine *e) {
+    if (!e->trace_on || e->trace_n >= e->trace_cap) return nullptr;
+    return e->trace_buf + 8 * (e->trace_n++);
 }
 
 struct DeviceGuard {
@@ -179,6 +189,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         g.out = e->qkv;
         g.epi = GEMV_STORE;
         g.status = e->status;
+        g.late_launch = (M == 1);  // lets the decode attention read n_past / cached K,V early
         if (l == 0) {
             g.embed_table = e->tok_embd;
             g.embed_ids = first_ids;
@@ -187,6 +198,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         } else {
             g.x = e->x;
         }
+        g.trace = next_trace(e);
         B200_TRY(mark(e, "qkv_gemv", gemv_launch(g, st, pdl)));
 
         QkNormRopeArgs r;
@@ -239,10 +251,13 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         a.freq = e->freq;
         a.eps = e->c.rms_eps;
         a.n_ctx = e->c.kv_capacity;
-        if (M == 1)
+        if (M == 1) {
+            a.trace = next_trace(e);
+            a.early_kv = pdl;  // the QKV GEMV before it signals late (late_launch)
             B200_TRY(mark(e, "attn_decode", attn_decode_launch(a, e->attn_splits, st, pdl)));
-        else
+        } else {
             B200_TRY(mark(e, "attn_prefill", attn_prefill_launch(a, st, pdl)));
+        }
 
         GemvArgs o;
         o.w = w.wo;
@@ -254,6 +269,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         o.residual = e->x;
         o.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
         o.status = e->status;
+        o.trace = next_trace(e);
         B200_TRY(mark(e, "o_proj_gemv", gemv_launch(o, st, pdl)));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
 
@@ -268,6 +284,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         gu.out = e->h;
         gu.epi = GEMV_SWIGLU;
         gu.status = e->status;
+        gu.trace = next_trace(e);
         B200_TRY(mark(e, "gate_up_gemv", gemv_launch(gu, st, pdl)));
 
         GemvArgs dn;
@@ -280,6 +297,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         dn.residual = e->x;
         dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
         dn.status = e->status;
+        dn.trace = next_trace(e);
         B200_TRY(mark(e, "down_gemv", gemv_launch(dn, st, pdl)));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
     }
@@ -298,11 +316,11 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
     lm.counter = e->am_counter;
     lm.status = e->status;
     if (e->tp) {
-        lm.argmax_out = e->am_idx + 4096;     // local winner (scratch slot)
-        lm.best_val_out = e->am_val + 4096;
+        lm.argmax_out = e->am_idx + e->am_slots;     // local winner (scratch slot)
+        lm.best_val_out = e->am_val + e->am_slots;
         lm.idx_offset = e->vocab_off;
         B200_TRY(gemv_launch(lm, st, pdl));
-        B200_TRY(tp_select_token(e->tp, e->am_val + 4096, e->am_idx + 4096, e->tp_pairs, e->token, e->token_log,
+        B200_TRY(tp_select_token(e->tp, e->am_val + e->am_slots, e->am_idx + e->am_slots, e->tp_pairs, e->token, e->token_log,
                                  e->log_pos, e->log_cap, e->n_past_dev, n_past_add, st));
     } else {
         lm.argmax_out = e->token;
@@ -311,6 +329,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         lm.log_cap = e->log_cap;
         lm.n_past = e->n_past_dev;
         lm.n_past_add = n_past_add;
+        lm.trace = next_trace(e);
         B200_TRY(mark(e, "lm_head_gemv", gemv_launch(lm, st, pdl)));
     }
     return B200_OK;
@@ -436,11 +455,11 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
     lm.counter = e->am_counter;
     lm.status = e->status;
     if (e->tp) {
-        lm.argmax_out = e->am_idx + 4096;
-        lm.best_val_out = e->am_val + 4096;
+        lm.argmax_out = e->am_idx + e->am_slots;
+        lm.best_val_out = e->am_val + e->am_slots;
         lm.idx_offset = e->vocab_off;
         B200_TRY(gemv_launch(lm, st, pdl));
-        B200_TRY(tp_select_token(e->tp, e->am_val + 4096, e->am_idx + 4096, e->tp_pairs, e->token, e->token_log,
+        B200_TRY(tp_select_token(e->tp, e->am_val + e->am_slots, e->am_idx + e->am_slots, e->tp_pairs, e->token, e->token_log,
                                  e->log_pos, e->log_cap, e->n_past_dev, n, st));
     } else {
         lm.argmax_out = e->token;
@@ -560,8 +579,11 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t o_log = take(e->log_cap), o_logpos = take(4);
     const size_t o_aws = off;
     off = align_up(off + e->attn_ws_bytes, A);
-    const size_t o_amv = take(4096 + 64), o_ami = take(4096 + 64), o_amc = take(64);
+    e->am_slots = gemv_argmax_slots(V, H);
+    const size_t o_amv = take(e->am_slots + 64), o_ami = take(e->am_slots + 64), o_amc = take(64);
     const size_t o_pairs = take(2 * W + 64);
+    e->trace_cap = 5 * c.n_layer + 8;
+    const size_t o_trace = take(2 * 8 * static_cast<int64_t>(e->trace_cap));
     e->act_bytes = off;
 
     cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
@@ -613,6 +635,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->am_idx = ai(o_ami);
     e->am_counter = reinterpret_cast<unsigned *>(e->act_arena + o_amc);
     e->tp_pairs = af(o_pairs);
+    e->trace_buf = reinterpret_cast<unsigned long long *>(e->act_arena + o_trace);
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
     std::vector<float> hf(D / 2);
@@ -912,6 +935,51 @@ int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *u
         us[i] = tot[i];
     }
     return n;
+}
+
+int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int max_kernels) {
+    if (!e || !e->finalized || !host_trace || max_kernels <= 0) return B200_ERR_INVALID_ARGUMENT;
+    if (e->tp || e->n_past + 1 > e->c.kv_capacity) return B200_ERR_NOT_SUPPORTED;
+    DeviceGuard dg(e->device);
+    cudaStream_t st = e->stream;
+    // One decode step captured and replayed exactly like the production graph,
+    // with every launch stamping the global timer; n_past and the token slot are
+    // restored afterwards.
+    int32_t saved[2];
+    B200_TRY(cudaMemcpyAsync(&saved[0], e->n_past_dev, 4, cudaMemcpyDeviceToHost, st));
+    B200_TRY(cudaMemcpyAsync(&saved[1], e->token, 4, cudaMemcpyDeviceToHost, st));
+    std::vector<unsigned long long> init(static_cast<size_t>(e->trace_cap) * 8, 0ull);
+    for (int i = 0; i < e->trace_cap; ++i) init[8 * i + 3] = ~0ull;
+    B200_TRY(cudaMemcpyAsync(e->trace_buf, init.data(), init.size() * 8, cudaMemcpyHostToDevice, st));
+    B200_TRY(cudaStreamSynchronize(st));
+    e->trace_on = true;
+    e->trace_n = 0;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t err = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    int rc = B200_OK;
+    if (err == cudaSuccess) {
+        rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+        err = cudaStreamEndCapture(st, &g);
+    }
+    e->trace_on = false;
+    const int n = e->trace_n;
+    if (err == cudaSuccess && rc == B200_OK) err = cudaGraphInstantiate(&ge, g, 0);
+    if (err == cudaSuccess && rc == B200_OK) err = cudaGraphLaunch(ge, st);
+    if (err == cudaSuccess && rc == B200_OK)
+        err = cudaMemcpyAsync(init.data(), e->trace_buf, static_cast<size_t>(n) * 64, cudaMemcpyDeviceToHost, st);
+    cudaError_t serr = cudaStreamSynchronize(st);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    cudaMemcpyAsync(e->n_past_dev, &saved[0], 4, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(e->token, &saved[1], 4, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+    if (rc != B200_OK) return rc;
+    if (err != cudaSuccess) return from_cuda(err);
+    if (serr != cudaSuccess) return from_cuda(serr);
+    const int out = n < max_kernels ? n : max_kernels;
+    std::memcpy(host_trace, init.data(), static_cast<size_t>(out) * 64);
+    return out;
 }
 
 void *b200_engine_stream(b200_engine *e) { return e ? e->stream : nullptr; }

@@ -11,6 +11,7 @@
 #include "gemv.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace b200 {
 
@@ -375,7 +376,25 @@ int gemv_grid_size(int64_t N, int epi) {
     return static_cast<int>(b200::min64(units, device_sm_count()));
 }
 
+int gemv_use_ring() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = std::getenv("B200_GEMV_IMPL");
+        v = (e && e[0] == 'r') ? 1 : 0;
+    }
+    return v;
+}
+
+int gemv_argmax_slots(int64_t N, int64_t K) {
+    return std::max(gemv_grid_size(N, GEMV_ARGMAX), gemv_direct_grid(N, K));
+}
+
 cudaError_t gemv_launch(const GemvArgs &a, cudaStream_t stream, bool pdl) {
+    if (!gemv_use_ring() && (a.N & 1) == 0) return gemv_direct_launch(a, stream, pdl);
+    return gemv_ring_launch(a, stream, pdl);
+}
+
+cudaError_t gemv_ring_launch(const GemvArgs &a, cudaStream_t stream, bool pdl) {
     if (a.M < 1 || a.M > 4 || (a.K & 3) || a.K <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == GEMV_ARGMAX && a.M != 1) return cudaErrorInvalidValue;
     if (a.epi == GEMV_SWIGLU && (a.N & 1)) return cudaErrorInvalidValue;

@@ -43,12 +43,21 @@ struct GemvArgs {
     int64_t idx_offset = 0;        // added to the winning row (vocab shard offset)
     float *best_val_out = nullptr; // optional: winning logit (tensor-parallel selection)
     int32_t *status = nullptr;
+    unsigned long long *trace = nullptr;  // optional step trace slot (common.cuh)
+    // Signal dependents only after this kernel's own dependency wait, so the next
+    // kernel may read, before its wait, anything produced two or more launches back.
+    bool late_launch = false;
 };
 
-// Launches the GEMV on `stream` (with programmatic dependent launch if pdl).
+// Launches the GEMV on `stream` (with programmatic dependent launch if pdl): the
+// direct-streaming kernel (gemv_direct.cu) for even N, else the bulk-copy ring.
 cudaError_t gemv_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
-// Number of CTAs the argmax variant uses for N rows (size of part_val / part_idx).
-int gemv_grid_size(int64_t N, int epi);
+cudaError_t gemv_direct_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
+cudaError_t gemv_ring_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
+int gemv_grid_size(int64_t N, int epi);      // CTAs of the ring kernel
+int gemv_direct_grid(int64_t N, int64_t K);  // CTAs of the direct kernel
+// Size of part_val / part_idx an ARGMAX launch over N rows of length K needs.
+int gemv_argmax_slots(int64_t N, int64_t K);
 int device_sm_count();
 
 }  // namespace b200
