@@ -106,9 +106,11 @@ void b200_rope_freqs(float theta, int64_t D, float *host_freq);
  * k[t*k_tok_stride + h*k_head_stride + d] (the reference cache is token-major:
  * k_tok_stride = Hkv*D, k_head_stride = D); out [D, Hq, Tq].
  * Key j is visible to query i iff j <= n_past + i; Tkv = n_past + Tq.
- * scale <= 0 selects 1/sqrt(D). Decode (Tq small) uses split-KV flash-decoding
- * with an in-kernel merge; prefill uses a tiled online-softmax kernel. Scratch for
- * the split-KV partials comes from `workspace` (b200_flash_attn_workspace_bytes).
+ * scale <= 0 selects 1/sqrt(D). Decode (Tq == 1) uses split-KV flash-decoding whose
+ * splits of one KV head form a thread-block cluster and merge through distributed
+ * shared memory; Tq > 1 uses a tiled online-softmax kernel. Neither needs global
+ * scratch today: `workspace` may be NULL (b200_flash_attn_workspace_bytes returns
+ * the size a future variant would need, currently 0 for decode).
  * Replaces CUDA_F32::compute_flash_attn (kernel_f32.hpp:24, kernel_f32.cu:452-511),
  * which mallocs an Hq*Tq*Tkv score matrix and synchronizes on every call. */
 int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D,

@@ -15,28 +15,11 @@ namespace {
 constexpr int kDecThreads = 128;
 constexpr int kDecTile = 32;
 
-struct DecWs {
-    unsigned *counters;  // [Hkv]
-    float *ml;           // [Hkv][S][G][2]
-    float *o;            // [Hkv][S][G][D]
-};
-
-__host__ __device__ inline DecWs dec_ws(void *base, int64_t Hq, int64_t Hkv, int S) {
-    DecWs w;
-    unsigned char *p = static_cast<unsigned char *>(base);
-    w.counters = reinterpret_cast<unsigned *>(p);
-    size_t off = (static_cast<size_t>(Hkv) * 4 + 255) & ~size_t(255);
-    w.ml = reinterpret_cast<float *>(p + off);
-    off += static_cast<size_t>(Hq) * S * 2 * 4;
-    off = (off + 255) & ~size_t(255);
-    w.o = reinterpret_cast<float *>(p + off);
-    return w;
-}
-
 // Split-KV flash decoding for one query token. CTA (s, kvh) covers keys
 // [L*s/S, L*(s+1)/S) of KV head kvh for its G query heads, in 32-key tiles
-// (double-buffered cp.async), with an online softmax; the last CTA of each KV
-// head to finish merges the S partial (m, l, o) triples in split order.
+// (double-buffered cp.async), with an online softmax. The S CTAs of a KV head
+// are one thread-block cluster; rank 0 merges the S partial (m, l, o) triples in
+// split order through distributed shared memory.
 //
 // Fused prologue (a.qkv set): q/k come raw from the QKV projection; the CTA
 // applies the per-head RMSNorm + RoPE to its q heads and the CTA holding
@@ -53,11 +36,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
     float *knew = qs + G * D;                  // [D] new token's k (normed, rotated)
     float *vnew = knew + D;                    // [D] new token's v
     float *P = vnew + D;                       // [G][32]
-    float *alpha_s = P + G * kDecTile;         // [G]
-    __shared__ unsigned s_ticket;
+    float *alpha_s = P + G * kDecTile;         // [G], then pm [G], pl [G], po [G][D]
 
     const TraceMark tm(a.trace);
     grid_launch_dependents();
+    prefetch_share_l2(a.next_w, a.next_w_bytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x;
     const int64_t kvh = blockIdx.y;
@@ -193,51 +176,46 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const AttnArgs
     }
     tm.at(5);
 
-    // partials
-    DecWs w = dec_ws(a.ws, a.Hq, a.Hkv, S);
-    const int64_t slot = (kvh * S + s) * G;
+    // Partials stay in this CTA's shared memory; the S CTAs of a KV head form one
+    // thread-block cluster and rank 0 merges them through distributed shared
+    // memory, in split order, between two cluster barriers.
+    float *pm = alpha_s + G;        // [G] running max
+    float *pl = pm + G;             // [G] running sum
+    float *po = pl + G;             // [G][D] unnormalised output
     if (warp < G && lane == 0) {
-        w.ml[(slot + warp) * 2 + 0] = m_run;
-        w.ml[(slot + warp) * 2 + 1] = l_run;
+        pm[warp] = m_run;
+        pl[warp] = l_run;
     }
 #pragma unroll
     for (int e = 0; e < DPT; ++e) {
         const int d = tid + e * kDecThreads;
         if (d < D)
 #pragma unroll
-            for (int g = 0; g < G; ++g) w.o[(slot + g) * D + d] = acc[g][e];
+            for (int g = 0; g < G; ++g) po[g * D + d] = acc[g][e];
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_ticket = atomicAdd(w.counters + kvh, 1u);
-    __syncthreads();
-    if (s_ticket != static_cast<unsigned>(S - 1)) {
-        tm.done();
-        return;
-    }
-    __threadfence();
-    // Last CTA of this KV head: merge the S splits in split order.
+    cluster_sync();
+    if (s == 0) {
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) {
-        const int d = tid + e * kDecThreads;
-        if (d >= D) continue;
+        for (int e = 0; e < DPT; ++e) {
+            const int d = tid + e * kDecThreads;
+            if (d >= D) continue;
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            float M = -INFINITY;
-            for (int ss = 0; ss < S; ++ss) M = fmaxf(M, __ldcg(w.ml + ((kvh * S + ss) * G + g) * 2));
-            float lsum = 0.f, o = 0.f;
-            for (int ss = 0; ss < S; ++ss) {
-                const int64_t sl = (kvh * S + ss) * G + g;
-                const float ms = __ldcg(w.ml + sl * 2);
-                if (ms == -INFINITY) continue;
-                const float f = expf(ms - M);
-                lsum = fmaf(f, __ldcg(w.ml + sl * 2 + 1), lsum);
-                o = fmaf(f, __ldcg(w.o + sl * D + d), o);
+            for (int g = 0; g < G; ++g) {
+                float M = -INFINITY;
+                for (int r = 0; r < S; ++r) M = fmaxf(M, ld_dsmem(dsmem_addr(pm + g, r)));
+                float lsum = 0.f, o = 0.f;
+                for (int r = 0; r < S; ++r) {
+                    const float ms = ld_dsmem(dsmem_addr(pm + g, r));
+                    if (ms == -INFINITY) continue;
+                    const float f = expf(ms - M);
+                    lsum = fmaf(f, ld_dsmem(dsmem_addr(pl + g, r)), lsum);
+                    o = fmaf(f, ld_dsmem(dsmem_addr(po + g * D + d, r)), o);
+                }
+                a.out[(kvh * G + g) * D + d] = o / lsum;
             }
-            a.out[(kvh * G + g) * D + d] = o / lsum;
         }
     }
-    if (tid == 0) w.counters[kvh] = 0u;
+    cluster_sync();  // peers keep their shared memory until rank 0 has read it
     tm.done();
 }
 
@@ -413,15 +391,34 @@ __global__ void __launch_bounds__(kPreThreads, 1) attn_prefill_kernel(const Attn
 
 template <int D, int G>
 cudaError_t dec_launch(const AttnArgs &a, int S, cudaStream_t stream, bool pdl) {
-    const size_t smem = (4 * kDecTile * (D + 4) + G * D + 2 * D + G * kDecTile + G) * sizeof(float);
+    const size_t smem =
+        (4 * kDecTile * (D + 4) + G * D + 2 * D + G * kDecTile + G + 2 * G + G * D) * sizeof(float);
     auto kern = attn_decode_kernel<D, G>;
     static bool configured = false;  // one instance per template instantiation
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    return b200_launch(kern, dim3(S, static_cast<unsigned>(a.Hkv)), dim3(kDecThreads), smem, stream, pdl, a, S);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, static_cast<unsigned>(a.Hkv));
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, S);
 }
 
 template <int D, int G>
@@ -470,24 +467,18 @@ bool strides_ok(const AttnArgs &a) {
 }  // namespace
 
 int attn_decode_splits(int64_t max_len) {
-    // One wave of CTAs over the KV heads for long contexts, fewer for short ones.
+    // The splits of one KV head form a cluster (<= 16 CTAs, non-portable above 8):
+    // about one 64-key chunk per CTA for short contexts, 16 per KV head for long ones.
     int64_t s = (max_len + 63) / 64;
     if (s < 1) s = 1;
-    if (s > 18) s = 18;
+    if (s > 16) s = 16;
     return static_cast<int>(s);
 }
 
-size_t attn_decode_ws_bytes(int64_t D, int64_t Hq, int64_t Hkv, int splits) {
-    size_t off = (static_cast<size_t>(Hkv) * 4 + 255) & ~size_t(255);
-    off += static_cast<size_t>(Hq) * splits * 2 * 4;
-    off = (off + 255) & ~size_t(255);
-    off += static_cast<size_t>(Hq) * splits * D * 4;
-    return off;
-}
+size_t attn_decode_ws_bytes(int64_t, int64_t, int64_t, int) { return 0; }
 
 cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t stream, bool pdl) {
-    if (!strides_ok(a) || a.Tq != 1 || splits < 1) return cudaErrorInvalidValue;
-    if (a.ws_bytes < attn_decode_ws_bytes(a.D, a.Hq, a.Hkv, splits)) return cudaErrorInvalidValue;
+    if (!strides_ok(a) || a.Tq != 1 || splits < 1 || splits > 16) return cudaErrorInvalidValue;
     switch (a.D) {
         case 64: return dec_by_g<64>(a, splits, stream, pdl);
         case 128: return dec_by_g<128>(a, splits, stream, pdl);

@@ -32,6 +32,9 @@ struct AttnArgs {
     // (GemvArgs::late_launch): n_past and the cached K/V rows [0, n_past) are then
     // complete when this kernel starts and are read before its dependency wait.
     bool early_kv = false;
+    // Weights of the next kernel, prefetched into L2 by this kernel's CTAs.
+    const void *next_w = nullptr;
+    size_t next_w_bytes = 0;
 };
 
 // Decode (Tq == 1): fixed `splits` x Hkv CTAs, each a slice of [0, n_past+1),

@@ -174,11 +174,9 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
     a.ws_bytes = workspace_bytes;
     cudaStream_t st = as_stream(stream);
     if (Tq == 1) {
+        // split-KV decode; the splits of a KV head merge through distributed shared
+        // memory inside one thread-block cluster, so no workspace is used
         const int S = attn_decode_splits(Tkv);
-        if (!workspace || workspace_bytes < attn_decode_ws_bytes(D, Hq, Hkv, S)) return B200_ERR_INVALID_ARGUMENT;
-        // split counters start at zero (the kernel leaves them zeroed for the next call)
-        cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(Hkv) * 4, st);
-        if (e != cudaSuccess) return from_cuda(e);
         return from_cuda(attn_decode_launch(a, S, st, false));
     }
     return from_cuda(attn_prefill_launch(a, st, false));

@@ -137,6 +137,49 @@ B200_DEVICE uint64_t policy_evict_last() {
     return p;
 }
 
+// TMA-engine bulk prefetch of [p, p + bytes) into L2 (p and bytes 16-byte multiples).
+B200_DEVICE void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share of an L2 prefetch of a byte range split evenly over the grid
+// (one bulk prefetch per CTA, issued by thread 0).
+B200_DEVICE void prefetch_share_l2(const void *base, size_t bytes) {
+    if (!base || bytes == 0 || threadIdx.x != 0) return;
+    const size_t nblk = static_cast<size_t>(gridDim.x) * gridDim.y;
+    const size_t b = static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+    const size_t chunk = ((bytes + nblk - 1) / nblk + 15) & ~size_t(15);
+    const size_t off = b * chunk;
+    if (off >= bytes) return;
+    size_t len = bytes - off < chunk ? bytes - off : chunk;
+    len &= ~size_t(15);
+    const char *p = static_cast<const char *>(base) + off;
+    while (len > 0) {  // the bulk-prefetch size operand is 32-bit
+        const uint32_t n = len > (1u << 30) ? (1u << 30) : static_cast<uint32_t>(len);
+        prefetch_l2_bulk(p, n);
+        p += n;
+        len -= n;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters: hardware cluster barrier and distributed shared memory.
+// Every thread of every CTA in the cluster must execute each cluster_sync().
+B200_DEVICE void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
+B200_DEVICE uint32_t dsmem_addr(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+B200_DEVICE float ld_dsmem(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 // Named barrier over `threads` threads (a multiple of 32) with id 1..15.
 B200_DEVICE void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

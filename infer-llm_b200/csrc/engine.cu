@@ -19,6 +19,8 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <tuple>
+#include <utility>
 #include <vector>
 
 #include "attention.cuh"
@@ -177,6 +179,26 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
                        bool pdl) {
     cudaStream_t st = e->stream;
     const int H = e->H, D = e->D;
+    // Weights streamed by decode launch idx (per layer: qkv, attention, o, gate/up,
+    // down; then the LM head). Launch i prefetches launch i+2's weights into L2.
+    auto wspan = [&](int idx) -> std::pair<const void *, size_t> {
+        const int nl = e->c.n_layer;
+        if (M != 1) return {nullptr, 0};
+        if (idx >= 5 * nl) {  // an LM-head prefix (the rest streams in its own kernel)
+            const size_t lm = static_cast<size_t>(e->V) * H * 4, part = size_t(48) << 20;
+            const size_t off = (idx == 5 * nl) ? 0 : part;
+            if (off >= lm) return {nullptr, 0};
+            return {reinterpret_cast<const char *>(e->lm_head) + off, std::min(part, lm - off)};
+        }
+        const LayerW &lw = e->L[idx / 5];
+        switch (idx % 5) {
+            case 0: return {lw.wqkv, static_cast<size_t>(e->qkv_rows) * H * 4};
+            case 2: return {lw.wo, static_cast<size_t>(H) * e->Hq * D * 4};
+            case 3: return {lw.wgu, static_cast<size_t>(2) * e->F * H * 4};
+            case 4: return {lw.wdown, static_cast<size_t>(H) * e->F * 4};
+        }
+        return {nullptr, 0};
+    };
     for (int l = 0; l < e->c.n_layer; ++l) {
         const LayerW &w = e->L[l];
         GemvArgs g;
@@ -199,6 +221,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
             g.x = e->x;
         }
         g.trace = next_trace(e);
+        std::tie(g.next_w, g.next_w_bytes) = wspan(5 * l + 2);
         B200_TRY(mark(e, "qkv_gemv", gemv_launch(g, st, pdl)));
 
         QkNormRopeArgs r;
@@ -253,6 +276,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         a.n_ctx = e->c.kv_capacity;
         if (M == 1) {
             a.trace = next_trace(e);
+            std::tie(a.next_w, a.next_w_bytes) = wspan(5 * l + 3);
             a.early_kv = pdl;  // the QKV GEMV before it signals late (late_launch)
             B200_TRY(mark(e, "attn_decode", attn_decode_launch(a, e->attn_splits, st, pdl)));
         } else {
@@ -270,6 +294,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         o.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
         o.status = e->status;
         o.trace = next_trace(e);
+        std::tie(o.next_w, o.next_w_bytes) = wspan(5 * l + 4);
         B200_TRY(mark(e, "o_proj_gemv", gemv_launch(o, st, pdl)));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
 
@@ -285,6 +310,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         gu.epi = GEMV_SWIGLU;
         gu.status = e->status;
         gu.trace = next_trace(e);
+        std::tie(gu.next_w, gu.next_w_bytes) = wspan(5 * l + 5);
         B200_TRY(mark(e, "gate_up_gemv", gemv_launch(gu, st, pdl)));
 
         GemvArgs dn;
@@ -298,6 +324,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMV_STORE : GEMV_RESIDUAL;
         dn.status = e->status;
         dn.trace = next_trace(e);
+        std::tie(dn.next_w, dn.next_w_bytes) = wspan(5 * l + 6);
         B200_TRY(mark(e, "down_gemv", gemv_launch(dn, st, pdl)));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
     }
@@ -330,6 +357,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         lm.n_past = e->n_past_dev;
         lm.n_past_add = n_past_add;
         lm.trace = next_trace(e);
+        std::tie(lm.next_w, lm.next_w_bytes) = wspan(0);
         B200_TRY(mark(e, "lm_head_gemv", gemv_launch(lm, st, pdl)));
     }
     return B200_OK;

@@ -390,7 +390,10 @@ int gemv_argmax_slots(int64_t N, int64_t K) {
 }
 
 cudaError_t gemv_launch(const GemvArgs &a, cudaStream_t stream, bool pdl) {
-    if (!gemv_use_ring() && (a.N & 1) == 0) return gemv_direct_launch(a, stream, pdl);
+    if (!gemv_use_ring() && (a.N & 1) == 0) {
+        const cudaError_t e = gemv_direct_launch(a, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     return gemv_ring_launch(a, stream, pdl);
 }
 

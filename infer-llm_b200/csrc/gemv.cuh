@@ -47,6 +47,10 @@ struct GemvArgs {
     // Signal dependents only after this kernel's own dependency wait, so the next
     // kernel may read, before its wait, anything produced two or more launches back.
     bool late_launch = false;
+    // Weights of the next kernel in the step, prefetched into L2 by this kernel's
+    // CTAs before their dependency wait (keeps HBM busy across kernel boundaries).
+    const void *next_w = nullptr;
+    size_t next_w_bytes = 0;
 };
 
 // Launches the GEMV on `stream` (with programmatic dependent launch if pdl): the
@@ -55,7 +59,8 @@ cudaError_t gemv_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
 cudaError_t gemv_direct_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
 cudaError_t gemv_ring_launch(const GemvArgs &a, cudaStream_t stream, bool pdl);
 int gemv_grid_size(int64_t N, int epi);      // CTAs of the ring kernel
-int gemv_direct_grid(int64_t N, int64_t K);  // CTAs of the direct kernel
+int gemv_direct_ks(int64_t N, int64_t K);    // K-slices per row of the direct kernel
+int gemv_direct_grid(int64_t N, int64_t K, int M = 1, bool norm = true);  // its CTAs
 // Size of part_val / part_idx an ARGMAX launch over N rows of length K needs.
 int gemv_argmax_slots(int64_t N, int64_t K);
 int device_sm_count();
