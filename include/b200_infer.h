@@ -146,6 +146,25 @@ int b200_argmax(const float *logits, int64_t n, int32_t *out_id, void *workspace
                 size_t workspace_bytes, int32_t *dev_status, void *stream);
 size_t b200_argmax_workspace_bytes(int64_t n);
 
+/* Allocation-free b200_argmax. This entry point has no counterpart in the
+ * reference: it serves callers that cannot allocate a device workspace, such as a
+ * kernel seam that receives only tensors and a stream (the reference's
+ * CUDA_F32::compute_* has no workspace argument) or a host that must not call
+ * cudaMalloc between steps (an allocation synchronises the device). Its scratch
+ * is a fixed library-owned device array of B200_ARGMAX_NOALLOC_SCRATCH bytes,
+ * held by every GPU that loads the library until the process exits; the call
+ * itself allocates nothing. Limits: n <= B200_ARGMAX_NOALLOC_MAX_N (larger n is
+ * rejected with B200_ERR_INVALID_ARGUMENT). The first call on a device resolves
+ * the array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture on that device. All calls share the one array (the counter in it
+ * is cleared at the start of every call): calls that overlap on the GPU, on any
+ * streams of the same device, race and must be serialised by the caller.
+ * Results equal b200_argmax's. */
+#define B200_ARGMAX_NOALLOC_SCRATCH 8192
+#define B200_ARGMAX_NOALLOC_MAX_N 2147483647LL
+int b200_argmax_noalloc(const float *logits, int64_t n, int32_t *out_id, int32_t *dev_status,
+                        void *stream);
+
 /* ------------------------------------------------------------------------
  * Qwen3 engine: device-resident weights, KV cache and activation arenas, the
  * fused per-layer kernel sequence, CUDA-graph decode. It is the runtime behind

@@ -57,6 +57,7 @@ _SIGS = {
     "b200_copy": ([_vp, _vp, _sz, _vp], C.c_int),
     "b200_argmax": ([_vp, _i64, _vp, _vp, _sz, _vp, _vp], C.c_int),
     "b200_argmax_workspace_bytes": ([_i64], _sz),
+    "b200_argmax_noalloc": ([_vp, _i64, _vp, _vp, _vp], C.c_int),
     "b200_engine_create": ([_vp, C.c_int, _vp], C.c_int),
     "b200_engine_destroy": ([_vp], None),
     "b200_engine_memory": ([_vp, _vp, _vp, _vp], C.c_int),
