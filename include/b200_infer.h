@@ -181,7 +181,15 @@ typedef struct b200_qwen3_config {
     int32_t precision;     /* B200_PREC_* for prefill matrix products */
     /* tensor parallelism (1 = single GPU); rank/world index this process */
     int32_t tp_rank, tp_world;
+    /* decode step: B200_DECODE_AUTO (the faster of the two for this shape),
+     * B200_DECODE_MULTI (the multi-kernel chain) or B200_DECODE_SINGLE (the
+     * persistent single-launch kernel where the shape allows it, else multi) */
+    int32_t decode_mode;
 } b200_qwen3_config;
+
+#define B200_DECODE_AUTO 0
+#define B200_DECODE_MULTI 1
+#define B200_DECODE_SINGLE 2
 
 typedef struct b200_engine b200_engine;
 
@@ -207,6 +215,12 @@ int b200_engine_finalize(b200_engine *e);
 int b200_engine_reset(b200_engine *e);
 int64_t b200_engine_n_past(const b200_engine *e);
 
+/* Kernel launches of this library per decode step after finalize: 1 when the
+ * single-launch decode kernel runs the step, else the multi-kernel count
+ * (5 per layer + LM head, + 2 token-selection kernels under tensor parallelism;
+ * NCCL's own kernels not counted). < 0 on error. */
+int b200_engine_decode_launches(const b200_engine *e);
+
 /* Evaluates n tokens (prefill if n > 1, decode if n == 1) at positions
  * n_past..n_past+n-1, appends their K/V and samples greedily from the last row.
  * host_ids: host memory; host_last_logits (nullable): receives the last row [V];
@@ -230,9 +244,11 @@ int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *u
  * order (per layer: QKV GEMV, attention, o_proj, gate/up, down; then LM head),
  * 8 global-timer words in ns: [CTA 0 start, CTA 0 after its dependency wait,
  * last CTA end, first CTA start of any CTA, CTA 0 after its prologue, CTA 0
- * after its main loop, 0, 0]. Returns the
- * number of launches written (<= max_kernels) or < 0. The step leaves n_past
- * and the token unchanged. */
+ * after its main loop, 0, 0]. With the single-launch decode kernel the entries
+ * are its phases in the same order, stamped by CTA 0: [0, 0, after the grid
+ * barrier that ends the phase, phase start, after the input load, after the
+ * main loop, 0, 0]. Returns the number of entries written (<= max_kernels) or
+ * < 0. The step leaves n_past and the token unchanged. */
 int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int max_kernels);
 
 /* Raw handles for in-process callers (bench / tests): the engine's stream and

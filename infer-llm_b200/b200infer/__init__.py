@@ -9,9 +9,9 @@ is missing or the device is not an sm_100 GPU, calls fail loudly.
 from .capi import (B200Error, lib, lib_path, build, mul_mat, rms_norm, rope, qk_norm_rope, flash_attn,
                   silu, mul, add, swiglu, get_rows, copy, argmax, rope_freqs, PREC_FFMA, PREC_TF32,
                   STATUS)
-from .engine import Engine
+from .engine import Engine, DECODE_AUTO, DECODE_MULTI, DECODE_SINGLE
 from . import gguf
 
 __all__ = ["B200Error", "lib", "lib_path", "build", "mul_mat", "rms_norm", "rope", "qk_norm_rope",
            "flash_attn", "silu", "mul", "add", "swiglu", "get_rows", "copy", "argmax", "rope_freqs",
-           "PREC_FFMA", "PREC_TF32", "STATUS", "Engine", "gguf"]
+           "PREC_FFMA", "PREC_TF32", "STATUS", "Engine", "DECODE_AUTO", "DECODE_MULTI", "DECODE_SINGLE", "gguf"]

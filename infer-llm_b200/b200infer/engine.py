@@ -15,7 +15,9 @@ class _Cfg(C.Structure):
                 ("n_ff", C.c_int32), ("n_ctx_train", C.c_int32), ("rope_theta", C.c_float),
                 ("rms_eps", C.c_float), ("tied", C.c_int32), ("kv_capacity", C.c_int32),
                 ("max_batch", C.c_int32), ("precision", C.c_int32), ("tp_rank", C.c_int32),
-                ("tp_world", C.c_int32)]
+                ("tp_world", C.c_int32), ("decode_mode", C.c_int32)]
+
+DECODE_AUTO, DECODE_MULTI, DECODE_SINGLE = 0, 1, 2
 
 
 def _chk(fn, rc):
@@ -31,11 +33,12 @@ class Engine:
     """
 
     def __init__(self, cfg: Qwen3Config, kv_capacity: int, max_batch: int = 512, device: int = 0,
-                 precision: int = PREC_FFMA, tp_rank: int = 0, tp_world: int = 1):
+                 precision: int = PREC_FFMA, tp_rank: int = 0, tp_world: int = 1,
+                 decode_mode: int = DECODE_AUTO):
         self.cfg = cfg
         self._c = _Cfg(cfg.n_vocab, cfg.n_embd, cfg.n_layer, cfg.n_head, cfg.n_head_kv, cfg.head_dim,
                        cfg.n_ff, cfg.n_ctx_train, cfg.rope_theta, cfg.rms_eps, int(cfg.tied),
-                       kv_capacity, max_batch, precision, tp_rank, tp_world)
+                       kv_capacity, max_batch, precision, tp_rank, tp_world, decode_mode)
         h = C.c_void_p()
         _chk("b200_engine_create", lib().b200_engine_create(C.byref(self._c), device, C.byref(h)))
         self.h = h
@@ -101,6 +104,14 @@ class Engine:
                                                           C.c_void_p(self._tok.ctypes.data)))
         return int(self._tok[0])
 
+    @property
+    def decode_launches(self) -> int:
+        """Kernel launches per decode step (1 = the single-launch decode kernel)."""
+        n = int(lib().b200_engine_decode_launches(self.h))
+        if n < 0:
+            raise B200Error("b200_engine_decode_launches", -n)
+        return n
+
     def generate(self, n_steps: int) -> np.ndarray:
         out = np.empty(max(n_steps, 1), np.int32)
         _chk("b200_engine_generate", lib().b200_engine_generate(self.h, n_steps, C.c_void_p(out.ctypes.data)))
@@ -109,7 +120,9 @@ class Engine:
     def trace(self) -> np.ndarray:
         """Device timeline of one graph-replayed decode step: (launches, 8) ns stamps
         [CTA0 start, CTA0 after dependency wait, last CTA end, first CTA start,
-        CTA0 after prologue, CTA0 after main loop, -, -]."""
+        CTA0 after prologue, CTA0 after main loop, -, -]; with the single-launch
+        decode kernel one row per phase [-, -, after the phase's grid barrier,
+        phase start, after the input load, after the main loop, -, -]."""
         cap = 5 * self.cfg.n_layer + 8
         buf = np.zeros((cap, 8), np.uint64)
         n = lib().b200_engine_trace_step(self.h, C.c_void_p(buf.ctypes.data), cap)

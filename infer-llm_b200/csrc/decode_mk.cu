@@ -1,0 +1,937 @@
+// Persistent decode megakernel: one cooperative launch runs a whole decode step
+// (28 layers x [QKV, attention, o_proj, gate/up, down] + LM head + greedy argmax)
+// with one CTA of 8 warps per SM.
+//
+// Weight streaming is decoupled from the activation dependency chain. The step's
+// static weight schedule (this CTA's row slice of every projection, layer after
+// layer, then the LM head) is cut into ring chunks of whole rows; chunk c belongs
+// to warp c % 8 and lives in shared-memory slot c % 16, so every warp refills its
+// own two slots with cp.async.bulk (TMA engine, mbarrier completion) the moment
+// it has read them. Copies therefore run 16 chunks (192 KB) ahead of consumption
+// and L2 bulk prefetches a further prefetch_chunks ahead, across phase boundaries
+// and grid barriers, so HBM keeps streaming while the CTA waits on activations.
+// Phases are separated by grid barriers (an L2 counter, bounded polling); each
+// phase reads its input activation through L2 (ld.global.cg), consumes its chunks
+// (one warp per chunk, several chunks in flight) and writes its outputs.
+//
+// Numerics match the multi-kernel path up to summation order: RMSNorm in double
+// with the reference's rounding, row sums and split partials combined in a fixed
+// order, so the step is deterministic.
+#include <algorithm>
+#include <cstdlib>
+
+#include "decode_mk.cuh"
+#include "gemv.cuh"
+#include "rope.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kCW = 8;               // consumer warps
+constexpr int kCT = kCW * 32;        // consumer threads
+// + one producer warpgroup (warp kCW streams weights, the other three exit).
+// Launched at 168 registers a thread (3 warps per SM sub-partition); the producer
+// warpgroup drops to kProdRegs and the consumers grow to kConsRegs:
+// 4*32*kProdRegs + 8*32*kConsRegs == 12*32*168.
+constexpr int kThreads = kCT + 128;
+constexpr int kProdRegs = 72;
+constexpr int kConsRegs = 216;
+static_assert(4 * kProdRegs + 8 * kConsRegs == 12 * 168, "register split must equal the launch total");
+constexpr int kStageFloats = 3072;   // 12 KB per ring stage (whole rows)
+constexpr int kStages = 16;
+// A ring slot is always read by the same warp (chunk c -> warp c % kCW, slot
+// c % kStages), so a warp waits on a slot's full barrier only after it consumed
+// the slot's previous chunk itself: the barrier is never two phases behind.
+static_assert(kStages % kCW == 0, "ring slots must map to a fixed consumer warp");
+constexpr int kMaxRpc = 8;           // rows per ring chunk at most
+constexpr int kMaxK = 3072;          // largest projection input (= one ring stage)
+constexpr int kMaxLayers = 40;
+constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
+constexpr int kMaxSplits = 18;
+constexpr int64_t kDefaultPrefetchKB = 256;
+enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_PER_LAYER = 5 };
+
+struct PhaseW {
+    const float *w;
+    int64_t N, K;
+    int unit;  // 2: rows come in (gate, up) pairs
+};
+
+// The layer table, copied to shared memory at kernel start: the ring cursors cross
+// phases constantly and every phase starts from a layer pointer, so none of them
+// may wait on a global load to find its matrix or norm weights.
+__shared__ MkLayer s_layers[kMaxLayers];
+
+B200_DEVICE PhaseW phase_w(const MkParams &p, int l, int ph) {
+    if (l == p.n_layer) return {p.lm_head, p.V, p.H, 1};
+    switch (ph) {
+        case PH_QKV: return {s_layers[l].wqkv, static_cast<int64_t>(p.Hq + 2 * p.Hkv) * p.D, p.H, 1};
+        case PH_O: return {s_layers[l].wo, p.H, static_cast<int64_t>(p.Hq) * p.D, 1};
+        case PH_GU: return {s_layers[l].wgu, 2 * static_cast<int64_t>(p.F), p.H, 2};
+        case PH_DOWN: return {s_layers[l].wdown, p.H, p.F, 1};
+    }
+    return {nullptr, 0, 0, 1};
+}
+
+// Rows per ring chunk: as many whole rows as one stage holds, at most kMaxRpc.
+B200_HOST_DEVICE int rpc_for(int64_t K, int /*unit*/) {
+    const int64_t r = kStageFloats / K;
+    return static_cast<int>(r < kMaxRpc ? r : kMaxRpc);
+}
+
+B200_DEVICE void rows_of(int64_t N, int unit, int b, int G, int64_t &r0, int64_t &r1) {
+    const int64_t units = N / unit;
+    r0 = units * b / G * unit;
+    r1 = units * (b + 1) / G * unit;
+}
+
+// Walks this CTA's weight schedule chunk by chunk, in consumption order: per layer
+// the QKV, o_proj, gate/up and down row slices (attention streams no weights), then
+// the LM head. A chunk is rpc whole rows (at most one ring stage). Advancing by n
+// chunks costs O(1) per phase crossed.
+struct Cursor {
+    int l = 0, ph = 0, k = 0, nch = 0, rpc = 1;
+    int64_t r0 = 0, r1 = 0;  // this CTA's rows of the phase; the cursor is at chunk k of nch
+    PhaseW pw{};
+
+    B200_DEVICE void load_phase(const MkParams &p, int b, int G) {
+        pw = phase_w(p, l, ph);
+        rows_of(pw.N, pw.unit, b, G, r0, r1);
+        rpc = rpc_for(pw.K, pw.unit);
+        nch = static_cast<int>((r1 - r0 + rpc - 1) / rpc);
+    }
+    // Positions the cursor at chunk n of the schedule; false if there is none.
+    B200_DEVICE bool start(const MkParams &p, int b, int G, int n) {
+        l = 0;
+        ph = 0;
+        k = 0;
+        load_phase(p, b, G);
+        return advance(p, b, G, n);
+    }
+    // Moves n chunks on; false once past the LM head.
+    B200_DEVICE bool advance(const MkParams &p, int b, int G, int n) {
+        k += n;
+        while (k >= nch) {
+            if (l == p.n_layer) return false;
+            k -= nch;
+            ph += (ph + 1 == PH_ATTN) ? 2 : 1;
+            if (ph >= PH_PER_LAYER) {
+                ++l;
+                ph = 0;
+            }
+            load_phase(p, b, G);
+        }
+        return true;
+    }
+    B200_DEVICE uint32_t bytes() const {
+        return static_cast<uint32_t>(min64(rpc, r1 - r0 - static_cast<int64_t>(k) * rpc) * pw.K * 4);
+    }
+    B200_DEVICE const float *src() const { return pw.w + (r0 + static_cast<int64_t>(k) * rpc) * pw.K; }
+};
+
+B200_DEVICE unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int E>
+B200_DEVICE void ldcg_vec(const float *src, float (&v)[E]) {
+    if constexpr (E == 4) {
+        const float4 t = __ldcg(reinterpret_cast<const float4 *>(src));
+        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else {
+        static_assert(E == 2, "head_dim 64 or 128");
+        const float2 t = __ldcg(reinterpret_cast<const float2 *>(src));
+        v[0] = t.x, v[1] = t.y;
+    }
+}
+
+B200_DEVICE int status_set(const int32_t *s) { return *reinterpret_cast<const volatile int32_t *>(s); }
+
+constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s
+
+// Bounded wait on an mbarrier phase: abandoned as soon as any CTA has reported an
+// error (its peers may have stopped), and after kWaitNs (sets the timeout status).
+// status == nullptr: wait for this CTA's own copies in flight, ignoring errors.
+B200_DEVICE bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 63) {
+            if (status && status_set(status)) return false;
+            const uint64_t t = global_ns();
+            if (!t0) t0 = t;
+            else if (t - t0 > kWaitNs) break;
+        }
+    }
+    if (status) set_status(status, B200_DEV_TIMEOUT);
+    return false;
+}
+
+struct Smem {
+    uint64_t *full, *empty;  // [kStages] copy-complete / slot-read barriers
+    float *ring;   // [kStages][kStageFloats]
+    float *xs;     // [kMaxK] phase input activation
+    float *part;   // [kPartFloats]
+    float *qs;     // [kCW][D] per-warp rotated query
+    float *wpart;  // [kCW][D + 2] per-warp attention partial (o, m, l)
+};
+
+template <int D>
+struct Mk {
+    static constexpr int E = D / 32;  // head elements per lane
+    const MkParams &p;
+    const Smem &sm;
+    const int tid, warp, lane, b, G;
+
+    // ---- grid barrier over the consumer threads of every CTA (bounded polling).
+    B200_DEVICE bool grid_sync(unsigned &epoch) {
+        __shared__ int s_ok;
+        named_sync(1, kCT);
+        epoch += static_cast<unsigned>(G);
+        if (tid == 0) {
+            // release at gpu scope is cumulative: it orders every consumer thread's
+            // phase outputs (ordered before it by the CTA barrier above)
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+            bool ok = false, failed = false;
+            uint64_t t0 = 0;
+            for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
+                if (ld_acquire(p.bar) >= epoch) {
+                    ok = true;
+                    break;
+                }
+                if (status_set(p.status)) {  // another CTA gave up
+                    failed = true;
+                    break;
+                }
+                if ((i & 15) == 15) {
+                    const uint64_t t = global_ns();
+                    if (!t0) t0 = t;
+                    else if (t - t0 > kWaitNs) break;
+                }
+            }
+            if (!ok && !failed) set_status(p.status, B200_DEV_TIMEOUT);
+            s_ok = ok;
+        }
+        named_sync(1, kCT);
+        return s_ok != 0;
+    }
+
+    // ---- phase input: xs = src (optionally RMS-normalised with gamma), via L2.
+    // x and gamma loads are issued together (one L2 round trip), the sum of
+    // squares is reduced with a single CTA barrier.
+    B200_DEVICE void load_act(const float *src, int64_t K, const float *gamma, float *also_store) {
+        constexpr int kV = kMaxK / 4 / kCT;  // float4 per thread at most
+        __shared__ double s_red[kCW];
+        const int64_t K4 = K >> 2;
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+        float4 v[kV], g[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int64_t i = tid + j * kCT;
+            if (i < K4) {
+                v[j] = __ldcg(s4 + i);
+                if (gamma) g[j] = __ldg(g4 + i);
+            }
+        }
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int64_t i = tid + j * kCT;
+            if (i < K4) {
+                if (also_store) reinterpret_cast<float4 *>(also_store)[i] = v[j];
+                const float q0 = v[j].x * v[j].x, q1 = v[j].y * v[j].y, q2 = v[j].z * v[j].z, q3 = v[j].w * v[j].w;
+                ss += static_cast<double>(q0);
+                ss += static_cast<double>(q1);
+                ss += static_cast<double>(q2);
+                ss += static_cast<double>(q3);
+            }
+        }
+        float sc = 1.f;
+        if (gamma) {
+            ss = warp_sum(ss);
+            if (lane == 0) s_red[warp] = ss;
+            named_sync(1, kCT);
+            double t = 0.0;  // every thread sums the warp totals in the same order
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) t += s_red[w];
+            sc = rms_scale_from_sumsq(t, K, p.eps);
+        }
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int64_t i = tid + j * kCT;
+            if (i < K4) {
+                float4 y = v[j];
+                if (gamma) {
+                    y.x = __fmul_rn(__fmul_rn(y.x, sc), g[j].x);
+                    y.y = __fmul_rn(__fmul_rn(y.y, sc), g[j].y);
+                    y.z = __fmul_rn(__fmul_rn(y.z, sc), g[j].z);
+                    y.w = __fmul_rn(__fmul_rn(y.w, sc), g[j].w);
+                }
+                reinterpret_cast<float4 *>(sm.xs)[i] = y;
+            }
+        }
+        named_sync(1, kCT);
+    }
+
+    // ---- R rows of one ring chunk against x (both in shared memory): each lane
+    // takes float4 columns lane, lane + 32, ...; U columns per row are loaded
+    // together (U * (R + 1) shared loads in flight) and accumulated per component
+    // so no FMA waits on the previous one. Releases the stage, then reduces the R
+    // row sums across the warp (fixed order) into dst[0..R).
+    template <int R>
+    B200_DEVICE void chunk_rows(const float4 *w4, const float4 *x4, int64_t K4, uint64_t *empty, float *dst) {
+        constexpr int U = R == 1 ? 8 : (R <= 3 ? 4 : 2);
+        float4 a[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) a[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t i0 = lane; i0 < K4; i0 += 32 * U) {
+            float4 xv[U], wv[R][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t i = i0 + 32 * u;
+                xv[u] = i < K4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < R; ++r) wv[r][u] = i < K4 ? w4[r * K4 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    a[r].x = fmaf(wv[r][u].x, xv[u].x, a[r].x);
+                    a[r].y = fmaf(wv[r][u].y, xv[u].y, a[r].y);
+                    a[r].z = fmaf(wv[r][u].z, xv[u].z, a[r].z);
+                    a[r].w = fmaf(wv[r][u].w, xv[u].w, a[r].w);
+                }
+        }
+        __syncwarp();  // the stage is read: hand it back to the producer
+        if (lane == 0) mbar_arrive(empty);
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = (a[r].x + a[r].y) + (a[r].z + a[r].w);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) dst[r] = acc[r];
+        }
+    }
+
+    // ---- consume this CTA's ring chunks of one projection: chunk k of the phase
+    // (schedule chunk cc + k) belongs to warp (cc + k) % kCW, which computes its
+    // rpc whole rows (x from shared memory, one lane-strided pass, one warp
+    // reduction per row) while the other warps work on the next chunks, and
+    // releases the slot to the producer. Row sums -> sm.part.
+    B200_DEVICE bool consume(const PhaseW &pw, int64_t r0, int64_t r1, int &cc, int trace_idx) {
+        const bool tr = p.trace && b == 0;  // CTA 0 records its slowest warp's chunk waits
+        __shared__ unsigned long long s_wait, s_loop;
+        if (tr && tid == 0) s_wait = s_loop = 0;
+        uint64_t t_wait = 0;
+        const long long tl0 = tr ? clock64() : 0;
+        const int rpc = rpc_for(pw.K, pw.unit);
+        const int64_t K4 = pw.K >> 2;
+        const int64_t nch = (r1 - r0 + rpc - 1) / rpc;
+        const float4 *x4 = reinterpret_cast<const float4 *>(sm.xs);
+        __shared__ int s_fail;
+        if (tid == 0) s_fail = 0;
+        named_sync(1, kCT);
+        for (int64_t k = ((warp - cc) % kCW + kCW) % kCW; k < nch; k += kCW) {
+            const int c = cc + static_cast<int>(k);
+            const int s = c % kStages;
+            const long long tw0 = tr ? clock64() : 0;
+            if (!mbar_wait_bounded(&sm.full[s], (c / kStages) & 1, p.status)) {
+                s_fail = 1;
+                break;
+            }
+            if (tr) t_wait += clock64() - tw0;
+            const int64_t row = r0 + k * rpc;
+            const int rows = static_cast<int>(min64(rpc, r1 - row));
+            const float4 *w4 = reinterpret_cast<const float4 *>(sm.ring + static_cast<size_t>(s) * kStageFloats);
+            float *dst = sm.part + (row - r0);
+            switch (rows) {
+                case 1: chunk_rows<1>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 2: chunk_rows<2>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 3: chunk_rows<3>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 4: chunk_rows<4>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 5: chunk_rows<5>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 6: chunk_rows<6>(w4, x4, K4, &sm.empty[s], dst); break;
+                case 7: chunk_rows<7>(w4, x4, K4, &sm.empty[s], dst); break;
+                default: chunk_rows<8>(w4, x4, K4, &sm.empty[s], dst); break;
+            }
+        }
+        cc += static_cast<int>(nch);
+        if (tr && lane == 0) {
+            atomicMax(&s_wait, static_cast<unsigned long long>(t_wait));
+            atomicMax(&s_loop, static_cast<unsigned long long>(clock64() - tl0));
+        }
+        named_sync(1, kCT);
+        if (tr && tid == 0) {
+            p.trace[trace_idx * 8 + 1] = s_loop;        // slowest warp's ring loop, SM cycles
+            p.trace[trace_idx * 8 + 6] = s_wait;        // slowest warp's total chunk wait, SM cycles
+            p.trace[trace_idx * 8 + 7] = global_ns();   // all chunks consumed
+        }
+        return s_fail == 0;  // uniform over the CTA
+    }
+
+    B200_DEVICE float row_sum(int64_t lr) const { return sm.part[lr]; }
+
+    // Attention splits per KV head for L keys: about 32 keys per split, at most
+    // kMaxSplits and at most G / Hkv (one CTA per (KV head, split)).
+    B200_DEVICE int attn_splits(int64_t L) const {
+        const int S = static_cast<int>((L + 31) / 32);
+        return max(1, min(S, min(kMaxSplits, G / p.Hkv)));
+    }
+
+    // ---- attention for one (KV head, split): fused q/k norm + RoPE, KV append,
+    // online softmax over the split's keys in batches of kTB. The first batch of
+    // cached keys/values is in flight while the queries and the new token are
+    // normalised; the new token's k/v come from shared memory (the cache row is
+    // written for later steps only), so there is no fence on the path.
+    B200_DEVICE void attention(int layer, int64_t n_past) {
+        constexpr int kTB = 8;
+        const MkLayer &Lw = s_layers[layer];
+        const int Gq = p.Hq / p.Hkv;
+        const int64_t L = n_past + 1;
+        const int S = attn_splits(L);
+        if (b >= p.Hkv * S) return;
+        const int g = b / S, s = b % S;
+        const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
+        const bool last = (s == S - 1);
+        const int64_t tok = static_cast<int64_t>(p.Hkv) * D;  // cache token stride
+        const int qh = warp % Gq, sub = warp / Gq, nsub = kCW / Gq;
+        const int h = g * Gq + qh;
+        const int64_t t0 = j0 + (j1 - j0) * sub / nsub, t1 = j0 + (j1 - j0) * (sub + 1) / nsub;
+        const float *kb = Lw.kc + g * D + lane * E, *vb = Lw.vc + g * D + lane * E;
+        float *kn = sm.part, *vn = sm.part + D;  // the new token's k, v
+        float kv[kTB][E], vv[kTB][E];
+        auto load_batch = [&](int64_t t, int n) {
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                if (j < n && t + j != n_past) {
+                    ldcg_vec(kb + (t + j) * tok, kv[j]);
+                    ldcg_vec(vb + (t + j) * tok, vv[j]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) kv[j][e] = vv[j][e] = 0.f;
+                }
+            }
+        };
+        load_batch(t0, static_cast<int>(min64(kTB, t1 - t0)));
+        if (last && warp == 0) {  // new token k: normalised + rotated
+            warp_norm_rope_head<E, true>(p.qkv + (p.Hq + g) * D, Lw.k_norm, p.freq, n_past, p.eps, kn);
+            __syncwarp();
+            float *dst = Lw.kc + n_past * tok + g * D;
+            for (int d = lane; d < D; d += 32) dst[d] = kn[d];
+        } else if (last && warp == 1) {  // new token v as is
+            const float *vsrc = p.qkv + (p.Hq + p.Hkv + g) * D;
+            float *vdst = Lw.vc + n_past * tok + g * D;
+            for (int d = lane; d < D; d += 32) {
+                const float v = __ldcg(vsrc + d);
+                vn[d] = v;
+                vdst[d] = v;
+            }
+        }
+        warp_norm_rope_head<E, true>(p.qkv + h * D, Lw.q_norm, p.freq, n_past, p.eps, sm.qs + warp * D);
+        named_sync(1, kCT);
+        float q[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) q[e] = sm.qs[warp * D + lane * E + e];
+        const float scale = 1.0f / sqrtf(static_cast<float>(D));
+        float m = -INFINITY, l = 0.f, o[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = 0.f;
+        for (int64_t t = t0; t < t1; t += kTB) {
+            const int n = static_cast<int>(min64(kTB, t1 - t));
+            if (t != t0) load_batch(t, n);
+            if (n_past >= t && n_past < t + n) {  // patch in the new token
+                const int j = static_cast<int>(n_past - t);
+#pragma unroll
+                for (int jj = 0; jj < kTB; ++jj)
+                    if (jj == j) {
+#pragma unroll
+                        for (int e = 0; e < E; ++e) {
+                            kv[jj][e] = kn[lane * E + e];
+                            vv[jj][e] = vn[lane * E + e];
+                        }
+                    }
+            }
+            float sc[kTB];
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; ++e) d = fmaf(q[e], kv[j][e], d);
+                sc[j] = d;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int j = 0; j < kTB; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], off);
+            float bm = m;
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                sc[j] = j < n ? sc[j] * scale : -INFINITY;
+                bm = fmaxf(bm, sc[j]);
+            }
+            const float corr = (m == -INFINITY) ? 0.f : expf(m - bm);
+            l *= corr;
+#pragma unroll
+            for (int e = 0; e < E; ++e) o[e] *= corr;
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                if (j < n) {
+                    const float pr = expf(sc[j] - bm);
+                    l += pr;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) o[e] = fmaf(pr, vv[j][e], o[e]);
+                }
+            }
+            m = bm;
+        }
+        float *wp = sm.wpart + warp * (D + 2);
+#pragma unroll
+        for (int e = 0; e < E; ++e) wp[lane * E + e] = o[e];
+        if (lane == 0) {
+            wp[D] = m;
+            wp[D + 1] = l;
+        }
+        named_sync(1, kCT);
+        // combine the token sub-ranges of each head in order -> split partial in L2
+        for (int i = tid; i < Gq * D; i += kCT) {
+            const int hh = i / D, d = i % D;
+            float M = -INFINITY;
+            for (int u = 0; u < nsub; ++u) M = fmaxf(M, sm.wpart[(u * Gq + hh) * (D + 2) + D]);
+            float lsum = 0.f, os = 0.f;
+            for (int u = 0; u < nsub; ++u) {
+                const float *w = sm.wpart + (u * Gq + hh) * (D + 2);
+                if (w[D] == -INFINITY) continue;
+                const float f = expf(w[D] - M);
+                lsum = fmaf(f, w[D + 1], lsum);
+                os = fmaf(f, w[d], os);
+            }
+            const int64_t sh = static_cast<int64_t>(s) * p.Hq + g * Gq + hh;
+            p.attn_part[sh * D + d] = os;
+            if (d == 0) {
+                float *ml = p.attn_part + static_cast<int64_t>(kMaxSplits) * p.Hq * D + sh * 2;
+                ml[0] = M;
+                ml[1] = lsum;
+            }
+        }
+    }
+
+    // ---- o_proj input: merge the attention splits (split order) into xs. The
+    // first kSG splits' partial outputs (float4 slices per thread) are in flight
+    // together with every split's (m, l): one L2 round trip up to kSG splits.
+    B200_DEVICE void merge_attention(int64_t n_past) {
+        constexpr int kV = kMaxK / 4 / kCT;  // float4 per thread at most
+        constexpr int kSG = 6;               // splits loaded per round
+        const int S = attn_splits(n_past + 1);
+        const int Hq = p.Hq;
+        const float *ml = p.attn_part + static_cast<int64_t>(kMaxSplits) * Hq * D;
+        const int n4 = Hq * D / 4;
+        const float4 *o4 = reinterpret_cast<const float4 *>(p.attn_part);
+        float4 ov[kSG][kV];
+        auto load_group = [&](int s0) {
+#pragma unroll
+            for (int j = 0; j < kSG; ++j)
+#pragma unroll
+                for (int v = 0; v < kV; ++v) {
+                    const int i4 = tid + v * kCT;
+                    ov[j][v] = (s0 + j < S && i4 < n4) ? __ldcg(o4 + static_cast<int64_t>(s0 + j) * n4 + i4)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+        };
+        load_group(0);
+        float *sw = sm.part;                      // [S][Hq]: m, then the split weight
+        float *sl = sm.part + kMaxSplits * Hq;    // [S][Hq]: l
+        float *sden = sl + kMaxSplits * Hq;       // [Hq]: sum of weighted l
+        for (int i = tid; i < S * Hq; i += kCT) {
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
+            sw[i] = v.x;
+            sl[i] = v.y;
+        }
+        named_sync(1, kCT);
+        for (int hh = tid; hh < Hq; hh += kCT) {
+            float M = -INFINITY;
+            for (int s = 0; s < S; ++s) M = fmaxf(M, sw[s * Hq + hh]);
+            float lsum = 0.f;
+            for (int s = 0; s < S; ++s) {
+                const float ms = sw[s * Hq + hh];
+                const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+                if (ms != -INFINITY) lsum = fmaf(f, sl[s * Hq + hh], lsum);
+                sw[s * Hq + hh] = f;
+            }
+            sden[hh] = lsum;
+        }
+        named_sync(1, kCT);
+        float4 acc[kV];
+#pragma unroll
+        for (int v = 0; v < kV; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < S; s0 += kSG) {
+            if (s0) load_group(s0);
+#pragma unroll
+            for (int j = 0; j < kSG; ++j)
+#pragma unroll
+                for (int v = 0; v < kV; ++v) {
+                    const int i4 = tid + v * kCT;
+                    if (s0 + j < S && i4 < n4) {
+                        const float f = sw[(s0 + j) * Hq + i4 * 4 / D];
+                        acc[v].x = fmaf(f, ov[j][v].x, acc[v].x);
+                        acc[v].y = fmaf(f, ov[j][v].y, acc[v].y);
+                        acc[v].z = fmaf(f, ov[j][v].z, acc[v].z);
+                        acc[v].w = fmaf(f, ov[j][v].w, acc[v].w);
+                    }
+                }
+        }
+#pragma unroll
+        for (int v = 0; v < kV; ++v) {
+            const int i4 = tid + v * kCT;
+            if (i4 < n4) {
+                const float den = sden[i4 * 4 / D];
+                reinterpret_cast<float4 *>(sm.xs)[i4] =
+                    make_float4(acc[v].x / den, acc[v].y / den, acc[v].z / den, acc[v].w / den);
+            }
+        }
+        named_sync(1, kCT);
+    }
+};
+
+B200_DEVICE void stamp(const MkParams &p, int idx, int k) {
+    if (p.trace && threadIdx.x == 0 && blockIdx.x == 0) p.trace[idx * 8 + k] = global_ns();
+}
+
+template <int D>
+B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p);
+
+// The producer thread: streams the step's weight schedule through the ring (slot
+// c % kStages for chunk c, refilled as soon as its consumer warp releases it) and
+// keeps L2 bulk prefetches prefetch_chunks ahead of the copies; past the LM head
+// the prefetches warm the head of the schedule for the next step (same weights).
+// It never waits on activations, so HBM keeps streaming while the consumers sit in
+// attention or at a grid barrier. Every wait is bounded and abandoned on error.
+B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
+    const uint64_t pol = policy_evict_first();
+    Cursor cp, pf;
+    bool live = cp.start(p, b, G, 0);
+    bool pf_live = false, pf_wrapped = false;
+    if (live) {
+        pf = cp;
+        pf_live = true;
+    }
+    int cc = 0, pc = 0;
+    while (live) {
+        while (pc < cc + kStages + p.prefetch_chunks) {
+            if (!pf_live) {
+                if (pf_wrapped) break;
+                pf_live = pf.start(p, b, G, 0);
+                pf_wrapped = true;
+                if (!pf_live) break;
+            }
+            if (pc >= cc + kStages) prefetch_l2_bulk(pf.src(), pf.bytes());  // the ring covers the rest
+            ++pc;
+            pf_live = pf.advance(p, b, G, 1);
+        }
+        const int s = cc % kStages;
+        // (a consumer that stopped leaves its slot unreleased: the wait sees the
+        // status word then; no per-chunk global load on the issue path)
+        if (cc >= kStages && !mbar_wait_bounded(&sm.empty[s], ((cc / kStages) - 1) & 1, p.status)) break;
+        const uint32_t bytes = cp.bytes();
+        mbar_arrive_expect_tx(&sm.full[s], bytes);
+        bulk_g2s(sm.ring + static_cast<size_t>(s) * kStageFloats, cp.src(), bytes, &sm.full[s], pol);
+        ++cc;
+        live = cp.advance(p, b, G, 1);
+    }
+    // Before leaving, wait (bounded) for the copies still in flight into this
+    // CTA's shared memory: the last min(cc, kStages) issued chunks.
+    for (int c = max(0, cc - kStages); c < cc; ++c) mbar_wait_bounded(&sm.full[c % kStages], (c / kStages) & 1, nullptr);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    Smem sm;
+    sm.full = reinterpret_cast<uint64_t *>(smem_raw);
+    sm.empty = sm.full + kStages;
+    sm.ring = reinterpret_cast<float *>(smem_raw + 256);
+    sm.xs = sm.ring + kStages * kStageFloats;
+    sm.part = sm.xs + kMaxK;
+    sm.qs = sm.part + kPartFloats;
+    sm.wpart = sm.qs + kCW * D;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.x, G = gridDim.x;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);  // the one warp that reads the slot's chunk
+        }
+        fence_barrier_init();
+    }
+    {
+        constexpr int kWords = sizeof(MkLayer) / 8;
+        static_assert(sizeof(MkLayer) % 8 == 0, "layer table copied in 8-byte words");
+        const unsigned long long *src = reinterpret_cast<const unsigned long long *>(p.layers);
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(s_layers);
+        for (int i = tid; i < p.n_layer * kWords; i += kThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+
+    if (warp >= kCW) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
+        if (warp == kCW && lane == 0) produce(p, sm, b, G);
+        return;
+    }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
+    Mk<D> mk{p, sm, tid, warp, lane, b, G};
+    run_step<D>(mk, p);
+}
+
+template <int D>
+B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
+    const int tid = mk.tid, warp = mk.warp, lane = mk.lane, b = mk.b, G = mk.G;
+    // The argmax ticket counter starts at zero even after an aborted step; every
+    // ticket is taken after the first grid barrier, which orders it after this.
+    if (b == 0 && tid == 0) *p.am_counter = 0u;
+    unsigned epoch = 0;
+    int cc = 0;
+    const int64_t n_past = *p.n_past;
+    const int32_t token = *p.token;
+    bool ok = true;
+    if (n_past < 0 || n_past >= p.n_ctx) {
+        if (tid == 0) set_status(p.status, B200_DEV_BAD_POSITION);
+        ok = false;
+    }
+    const bool bad_tok = token < 0 || token >= p.V;  // V == vocabulary on one GPU
+    if (bad_tok) {
+        if (tid == 0) set_status(p.status, B200_DEV_BAD_TOKEN);
+        ok = false;
+    }
+    int64_t r0 = 0, r1 = 0;
+    for (int l = 0; l < p.n_layer && ok; ++l) {
+        const MkLayer &Lw = s_layers[l];
+        const int base = l * PH_PER_LAYER;
+        // QKV (layer 0 reads the embedding row and stores it as the residual)
+        stamp(p, base + PH_QKV, 3);
+        if (l == 0)
+            mk.load_act(p.tok_embd + static_cast<int64_t>(token) * p.H, p.H, Lw.attn_norm, b == 0 ? p.x : nullptr);
+        else
+            mk.load_act(p.x, p.H, Lw.attn_norm, nullptr);
+        stamp(p, base + PH_QKV, 4);
+        PhaseW pw = phase_w(p, l, PH_QKV);
+        rows_of(pw.N, 1, b, G, r0, r1);
+        ok = mk.consume(pw, r0, r1, cc, base + PH_QKV);
+        {
+            for (int64_t r = r0 + tid; r < r1; r += kCT) p.qkv[r] = mk.row_sum(r - r0);
+        }
+        stamp(p, base + PH_QKV, 5);
+        if (!ok || !mk.grid_sync(epoch)) break;
+        stamp(p, base + PH_QKV, 2);
+        // attention
+        stamp(p, base + PH_ATTN, 3);
+        mk.attention(l, n_past);
+        stamp(p, base + PH_ATTN, 5);
+        if (!mk.grid_sync(epoch)) break;
+        stamp(p, base + PH_ATTN, 2);
+        // o_proj + residual
+        stamp(p, base + PH_O, 3);
+        mk.merge_attention(n_past);
+        stamp(p, base + PH_O, 4);
+        pw = phase_w(p, l, PH_O);
+        rows_of(pw.N, 1, b, G, r0, r1);
+        ok = mk.consume(pw, r0, r1, cc, base + PH_O);
+        {
+            for (int64_t r = r0 + tid; r < r1; r += kCT) p.x[r] = mk.row_sum(r - r0) + __ldcg(p.x + r);
+        }
+        stamp(p, base + PH_O, 5);
+        if (!ok || !mk.grid_sync(epoch)) break;
+        stamp(p, base + PH_O, 2);
+        // gate/up + SwiGLU
+        stamp(p, base + PH_GU, 3);
+        mk.load_act(p.x, p.H, Lw.ffn_norm, nullptr);
+        stamp(p, base + PH_GU, 4);
+        pw = phase_w(p, l, PH_GU);
+        rows_of(pw.N, 2, b, G, r0, r1);
+        ok = mk.consume(pw, r0, r1, cc, base + PH_GU);
+        {
+            for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
+                const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
+                const float sg = gt / (1.0f + expf(-gt));
+                p.h[pr] = up * sg;
+            }
+        }
+        stamp(p, base + PH_GU, 5);
+        if (!ok || !mk.grid_sync(epoch)) break;
+        stamp(p, base + PH_GU, 2);
+        // down + residual
+        stamp(p, base + PH_DOWN, 3);
+        mk.load_act(p.h, p.F, nullptr, nullptr);
+        stamp(p, base + PH_DOWN, 4);
+        pw = phase_w(p, l, PH_DOWN);
+        rows_of(pw.N, 1, b, G, r0, r1);
+        ok = mk.consume(pw, r0, r1, cc, base + PH_DOWN);
+        {
+            for (int64_t r = r0 + tid; r < r1; r += kCT) p.x[r] = mk.row_sum(r - r0) + __ldcg(p.x + r);
+        }
+        stamp(p, base + PH_DOWN, 5);
+        if (!ok || !mk.grid_sync(epoch)) break;
+        stamp(p, base + PH_DOWN, 2);
+    }
+    if (!ok || status_set(p.status)) return;
+
+    // ---- LM head + greedy argmax (first maximum; NaN / +inf -> -1)
+    const int lm = p.n_layer * PH_PER_LAYER;
+    stamp(p, lm, 3);
+    mk.load_act(p.x, p.H, p.out_norm, nullptr);
+    stamp(p, lm, 4);
+    const PhaseW pw = phase_w(p, p.n_layer, 0);
+    rows_of(pw.N, 1, b, G, r0, r1);
+    if (!mk.consume(pw, r0, r1, cc, lm)) return;
+    float bv = -INFINITY;
+    int64_t bi = INT64_MAX;
+    bool bad = false;
+    for (int64_t r = r0 + tid; r < r1; r += kCT) {  // per thread: increasing rows
+        const float v = mk.row_sum(r - r0);
+        if (p.logits) p.logits[r] = v;
+        if (isnan(v) || v == INFINITY) bad = true;
+        if (v > bv) {
+            bv = v;
+            bi = r;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    __shared__ float s_bv[kCW];
+    __shared__ int64_t s_bi[kCW];
+    __shared__ int s_bad[kCW];
+    __shared__ unsigned s_ticket;
+    if (lane == 0) {
+        s_bv[warp] = bv;
+        s_bi[warp] = bi;
+        s_bad[warp] = bad;
+    }
+    named_sync(1, kCT);
+    if (tid == 0) {
+        float v = s_bv[0];
+        int64_t i = s_bi[0];
+        bool anyb = s_bad[0];
+        for (int w = 1; w < kCW; ++w) {
+            anyb |= s_bad[w] != 0;
+            if (s_bv[w] > v || (s_bv[w] == v && s_bi[w] < i)) {
+                v = s_bv[w];
+                i = s_bi[w];
+            }
+        }
+        p.am_val[b] = anyb ? NAN : v;
+        p.am_idx[b] = anyb ? -2 : (i == INT64_MAX ? -1 : static_cast<int32_t>(i));
+        __threadfence();
+        s_ticket = atomicAdd(p.am_counter, 1u);
+    }
+    named_sync(1, kCT);
+    stamp(p, lm, 5);
+    if (s_ticket != static_cast<unsigned>(G - 1)) return;
+    if (tid == 0) {
+        __threadfence();
+        float v = -INFINITY;
+        int32_t id = -1;
+        bool anyb = false;
+        for (int c = 0; c < G; ++c) {  // CTAs own increasing row ranges
+            const float cv = __ldcg(p.am_val + c);
+            const int32_t ci = __ldcg(p.am_idx + c);
+            if (ci == -2) anyb = true;
+            if (cv > v) {
+                v = cv;
+                id = ci;
+            }
+        }
+        if (anyb || id < 0) {
+            id = -1;
+            set_status(p.status, B200_DEV_BAD_LOGITS);
+        }
+        *p.token = id;
+        if (p.token_log) {
+            const int32_t q = *p.log_pos;
+            p.token_log[q % p.log_cap] = id;
+            *p.log_pos = q + 1;
+        }
+        *p.n_past = static_cast<int32_t>(n_past + 1);
+        *p.am_counter = 0u;
+        stamp(p, lm, 2);
+    }
+}
+
+size_t smem_bytes(int D) {
+    return 256 + static_cast<size_t>(kStages) * kStageFloats * 4 + static_cast<size_t>(kMaxK) * 4 +
+           static_cast<size_t>(kPartFloats) * 4 + static_cast<size_t>(kCW) * D * 4 +
+           static_cast<size_t>(kCW) * (D + 2) * 4;
+}
+
+}  // namespace
+
+int mk_grid() { return device_sm_count(); }
+
+// L2 prefetch distance per CTA beyond the ring, in ring chunks
+// (B200_MK_PREFETCH_KB overrides the default distance in KB).
+int mk_prefetch_chunks() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = std::getenv("B200_MK_PREFETCH_KB");
+        const long long kb = (e && *e) ? std::max(0LL, std::atoll(e)) : kDefaultPrefetchKB;
+        v = static_cast<int>(kb * 1024 / (kStageFloats * 4));
+    }
+    return v;
+}
+int mk_max_splits() { return kMaxSplits; }
+size_t mk_attn_part_floats(const MkParams &p) {
+    return static_cast<size_t>(kMaxSplits) * p.Hq * (p.D + 2);
+}
+
+bool mk_supported(const MkParams &p) {
+    if (p.D != 64 && p.D != 128) return false;
+    if (p.n_layer < 1 || p.n_layer > kMaxLayers) return false;
+    if (p.Hkv <= 0 || p.Hq % p.Hkv || kCW % (p.Hq / p.Hkv)) return false;
+    const int G = mk_grid();
+    if (p.Hkv > G) return false;
+    if (2 * kMaxSplits * p.Hq + p.Hq > kPartFloats) return false;  // merge scratch
+    const int64_t Ks[] = {p.H, static_cast<int64_t>(p.Hq) * p.D, p.F};
+    for (int64_t K : Ks)
+        if (K > kMaxK || (K & 3) || K < 64) return false;
+    // every projection: a chunk fits one ring stage, the per-CTA row sums fit sm.part
+    const int64_t Ns[] = {static_cast<int64_t>(p.Hq + 2 * p.Hkv) * p.D, p.H, 2 * static_cast<int64_t>(p.F), p.H, p.V};
+    const int64_t Kof[] = {p.H, static_cast<int64_t>(p.Hq) * p.D, p.H, p.F, p.H};
+    const int units[] = {1, 1, 2, 1, 1};
+    for (int i = 0; i < 5; ++i) {
+        const int rpc = rpc_for(Kof[i], units[i]);
+        if (rpc < 1 || rpc > kMaxRpc || static_cast<int64_t>(rpc) * Kof[i] > kStageFloats) return false;
+        const int64_t rows = ((Ns[i] / units[i] + G - 1) / G) * units[i] + 1;
+        if (rows > kPartFloats) return false;
+    }
+    return true;
+}
+
+cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
+    const size_t smem = smem_bytes(p.D);
+    void *kern = p.D == 64 ? reinterpret_cast<void *>(decode_mk_kernel<64>) : reinterpret_cast<void *>(decode_mk_kernel<128>);
+    // Per device and cheap: the launch is recorded once into the decode graph.
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p.bar, 0, sizeof(unsigned), stream);
+    if (e != cudaSuccess) return e;
+    MkParams args = p;
+    args.prefetch_chunks = mk_prefetch_chunks();
+    void *kargs[] = {&args};
+    return cudaLaunchCooperativeKernel(kern, dim3(mk_grid()), dim3(kThreads), kargs, smem, stream);
+}
+
+}  // namespace b200

@@ -1,0 +1,49 @@
+// Persistent single-launch decode step (one token through every layer + LM head).
+#pragma once
+
+#include "common.cuh"
+
+namespace b200 {
+
+struct MkLayer {
+    const float *attn_norm, *wqkv, *q_norm, *k_norm, *wo, *ffn_norm, *wgu, *wdown;
+    float *kc, *vc;  // KV object of the layer: K block [cap][Hkv][D], V block
+};
+
+struct MkParams {
+    const MkLayer *layers = nullptr;  // device array [n_layer]
+    int n_layer = 0;
+    int H = 0, D = 0, Hq = 0, Hkv = 0, F = 0, V = 0;
+    float eps = 0.f;
+    int64_t n_ctx = 0;                 // KV capacity (positions must stay below)
+    const float *tok_embd = nullptr, *out_norm = nullptr, *lm_head = nullptr, *freq = nullptr;
+    float *x = nullptr;                // residual [H]
+    float *qkv = nullptr;              // [(Hq + 2 Hkv) D]
+    float *attn_part = nullptr;        // [max_splits][Hq][D + 2] split partials (o, m, l)
+    float *h = nullptr;                // [F]
+    float *logits = nullptr;           // [V] or nullptr
+    int32_t *token = nullptr;          // in: token of this step; out: greedy next token
+    int32_t *n_past = nullptr;         // advanced by 1 at the end of the step
+    int32_t *status = nullptr;
+    int32_t *token_log = nullptr, *log_pos = nullptr;
+    int32_t log_cap = 0;
+    unsigned *bar = nullptr;           // grid-barrier counter, zero at launch
+    float *am_val = nullptr;           // [gridDim.x] per-CTA argmax partials
+    int32_t *am_idx = nullptr;
+    unsigned *am_counter = nullptr;    // zero at launch; the last CTA re-zeroes it
+    unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
+    int prefetch_chunks = 0;           // per CTA: L2 prefetch distance beyond the ring, in ring
+                                       // chunks (set by mk_launch)
+};
+
+// True if the megakernel supports this model shape on this device.
+bool mk_supported(const MkParams &p);
+int mk_max_splits();
+size_t mk_attn_part_floats(const MkParams &p);
+// Enqueues the zeroing of the barrier counter and the cooperative launch.
+cudaError_t mk_launch(const MkParams &p, cudaStream_t stream);
+int mk_grid();
+// L2 prefetch distance of each CTA ahead of its ring copies, in ring chunks.
+int mk_prefetch_chunks();
+
+}  // namespace b200

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_mk.cuh"
 #include "elementwise.cuh"
 #include "engine_tp.cuh"
 #include "gemm.cuh"
@@ -131,6 +132,10 @@ struct b200_engine {
     // per-op timing (b200_engine_profile_step): an event is recorded after each launch
     std::vector<cudaEvent_t> *prof_events = nullptr;
     std::vector<const char *> *prof_names = nullptr;
+    // single-launch decode step (decode_mk.cu)
+    bool use_mk = false;
+    MkParams mk;
+    MkLayer *mk_layers = nullptr;  // device table
 };
 
 namespace {
@@ -517,7 +522,14 @@ int check_status(b200_engine *e) {
 int build_graph(b200_engine *e) {
     if (e->graph_exec) return B200_OK;
     B200_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+    int rc = B200_OK;
+    if (e->use_mk) {
+        MkParams p = e->mk;
+        p.trace = nullptr;
+        rc = from_cuda(mk_launch(p, e->stream));
+    } else {
+        rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+    }
     cudaGraph_t g = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (rc != B200_OK) {
@@ -607,11 +619,17 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t o_log = take(e->log_cap), o_logpos = take(4);
     const size_t o_aws = off;
     off = align_up(off + e->attn_ws_bytes, A);
-    e->am_slots = gemv_argmax_slots(V, H);
+    e->am_slots = std::max(gemv_argmax_slots(V, H), mk_grid());
     const size_t o_amv = take(e->am_slots + 64), o_ami = take(e->am_slots + 64), o_amc = take(64);
     const size_t o_pairs = take(2 * W + 64);
     e->trace_cap = 5 * c.n_layer + 8;
     const size_t o_trace = take(2 * 8 * static_cast<int64_t>(e->trace_cap));
+    const size_t o_mkl = take(static_cast<int64_t>(sizeof(MkLayer) / 4 + 1) * NL);
+    MkParams shape;
+    shape.Hq = e->Hq;
+    shape.D = static_cast<int>(D);
+    const size_t o_apart = take(static_cast<int64_t>(mk_attn_part_floats(shape)));
+    const size_t o_mkbar = take(64);
     e->act_bytes = off;
 
     cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
@@ -664,6 +682,9 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->am_counter = reinterpret_cast<unsigned *>(e->act_arena + o_amc);
     e->tp_pairs = af(o_pairs);
     e->trace_buf = reinterpret_cast<unsigned long long *>(e->act_arena + o_trace);
+    e->mk_layers = reinterpret_cast<MkLayer *>(e->act_arena + o_mkl);
+    e->mk.attn_part = af(o_apart);
+    e->mk.bar = reinterpret_cast<unsigned *>(e->act_arena + o_mkbar);
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
     std::vector<float> hf(D / 2);
@@ -713,7 +734,7 @@ int b200_engine_set_weight(b200_engine *e, const char *name, const float *host, 
     if (e->finalized) return B200_ERR_INVALID_ARGUMENT;
     DeviceGuard dg(e->device);
     const b200_qwen3_config &c = e->c;
-    const int W = c.tp_world, r = c.tp_rank;
+    const int r = c.tp_rank;
     const int64_t H = e->H, D = e->D, F = e->F, V = e->V;
     const int64_t Hq_all = c.n_head, Hkv_all = c.n_head_kv;
     cudaStream_t st = e->stream;
@@ -826,6 +847,48 @@ int b200_engine_finalize(b200_engine *e) {
         return B200_ERR_INVALID_ARGUMENT;
     }
     if (e->c.tp_world > 1 && !e->tp) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    // Single-launch decode step where the shape allows it (one GPU only).
+    MkParams &p = e->mk;
+    p.n_layer = e->c.n_layer;
+    p.H = e->H;
+    p.D = e->D;
+    p.Hq = e->Hq;
+    p.Hkv = e->Hkv;
+    p.F = e->F;
+    p.V = e->V;
+    p.eps = e->c.rms_eps;
+    p.n_ctx = e->c.kv_capacity;
+    p.tok_embd = e->tok_embd;
+    p.out_norm = e->out_norm;
+    p.lm_head = e->lm_head;
+    p.freq = e->freq;
+    p.x = e->x;
+    p.qkv = e->qkv;
+    p.h = e->h;
+    p.logits = e->logits;  // V floats per step, so eval() can return logits from the graph step
+    p.token = e->token;
+    p.n_past = e->n_past_dev;
+    p.status = e->status;
+    p.token_log = e->token_log;
+    p.log_pos = e->log_pos;
+    p.log_cap = e->log_cap;
+    p.am_val = e->am_val;
+    p.am_idx = e->am_idx;
+    p.am_counter = e->am_counter;
+    p.layers = e->mk_layers;
+    // AUTO keeps the multi-kernel chain until the single-launch kernel is faster
+    // on the benchmark shape.
+    e->use_mk = e->c.decode_mode == B200_DECODE_SINGLE && e->c.tp_world == 1 && mk_supported(p) &&
+                mk_grid() <= e->am_slots;
+    if (e->use_mk) {
+        std::vector<MkLayer> tab(e->c.n_layer);
+        for (int l = 0; l < e->c.n_layer; ++l) {
+            const LayerW &w = e->L[l];
+            tab[l] = MkLayer{w.attn_norm, w.wqkv, w.q_norm, w.k_norm, w.wo, w.ffn_norm, w.wgu, w.wdown, w.kc, w.vc};
+        }
+        B200_TRY(cudaMemcpy(e->mk_layers, tab.data(), sizeof(MkLayer) * tab.size(), cudaMemcpyHostToDevice));
+    }
     e->finalized = true;
     return B200_OK;
 }
@@ -841,6 +904,12 @@ int b200_engine_reset(b200_engine *e) {
 
 int64_t b200_engine_n_past(const b200_engine *e) { return e ? e->n_past : -1; }
 
+int b200_engine_decode_launches(const b200_engine *e) {
+    if (!e || !e->finalized) return -B200_ERR_INVALID_ARGUMENT;
+    if (e->use_mk) return 1;
+    return 5 * e->c.n_layer + 1 + (e->tp ? 2 : 0);
+}
+
 int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *host_last_logits,
                      int32_t *host_token) {
     if (!e || !host_ids || n <= 0) return B200_ERR_INVALID_ARGUMENT;
@@ -853,7 +922,7 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
     cudaStream_t st = e->stream;
     const bool want_logits = host_last_logits != nullptr;
     int rc;
-    if (n == 1 && !want_logits && e->c.tp_world == 1) {
+    if (n == 1 && e->c.tp_world == 1 && (!want_logits || e->use_mk)) {
         // graph-replayed decode: the token slot is the embedding input
         e->pinned_io[0] = host_ids[0];
         B200_TRY(cudaMemcpyAsync(e->token, e->pinned_io, 4, cudaMemcpyHostToDevice, st));
@@ -986,12 +1055,20 @@ int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int m
     cudaGraphExec_t ge = nullptr;
     cudaError_t err = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
     int rc = B200_OK;
+    int n = 0;
     if (err == cudaSuccess) {
-        rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+        if (e->use_mk) {
+            MkParams p = e->mk;
+            p.trace = e->trace_buf;
+            rc = from_cuda(mk_launch(p, st));
+            n = 5 * e->c.n_layer + 1;
+        } else {
+            rc = enqueue_small_step(e, e->token, 1, false, 1, true);
+        }
         err = cudaStreamEndCapture(st, &g);
     }
     e->trace_on = false;
-    const int n = e->trace_n;
+    if (!e->use_mk) n = e->trace_n;
     if (err == cudaSuccess && rc == B200_OK) err = cudaGraphInstantiate(&ge, g, 0);
     if (err == cudaSuccess && rc == B200_OK) err = cudaGraphLaunch(ge, st);
     if (err == cudaSuccess && rc == B200_OK)

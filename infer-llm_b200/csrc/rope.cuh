@@ -12,7 +12,9 @@ namespace b200 {
 // products summed in double (cpu_backend.cpp:369-376), y = (x * scale) * gamma,
 // angle = float(double(pos) * freq_j) (graph.cpp:119-131), separately rounded
 // products in the rotation (cpu_backend.cpp:514-519).
-template <int E>
+// L2_ONLY: read `src` with ld.global.cg (for data other SMs rewrote since this SM
+// last read the same address, e.g. inside a persistent kernel).
+template <int E, bool L2_ONLY = false>
 B200_DEVICE void warp_norm_rope_head(const float *__restrict__ src, const float *__restrict__ gamma,
                                      const float *__restrict__ freq, int64_t pos, float eps,
                                      float *__restrict__ dst) {
@@ -22,7 +24,7 @@ B200_DEVICE void warp_norm_rope_head(const float *__restrict__ src, const float 
     double ss = 0.0;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        v[e] = src[lane * E + e];
+        v[e] = L2_ONLY ? __ldcg(src + lane * E + e) : src[lane * E + e];
         const float sq = v[e] * v[e];
         ss += static_cast<double>(sq);
     }

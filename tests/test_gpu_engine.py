@@ -28,9 +28,14 @@ def tiny(tmp_path_factory):
     return path
 
 
-def test_tiny_matches_reference_golden(cuda, golden, tiny):
+MODES = pytest.mark.parametrize("mode", [B.DECODE_SINGLE, B.DECODE_MULTI], ids=["single_launch", "multi_kernel"])
+
+
+@MODES
+def test_tiny_matches_reference_golden(cuda, golden, tiny, mode):
     cfg = G.QWEN3_TINY
-    eng = B.Engine(cfg, kv_capacity=64, max_batch=16).load_gguf(tiny).finalize()
+    eng = B.Engine(cfg, kv_capacity=64, max_batch=16, decode_mode=mode).load_gguf(tiny).finalize()
+    assert eng.decode_launches == (1 if mode == B.DECODE_SINGLE else 5 * cfg.n_layer + 1)
     logits = np.empty(cfg.n_vocab, np.float32)
     tok = eng.eval(golden["e2e_prompt"], logits)
     assert rel_err(logits, golden["e2e_logits_prefill"]) <= 1e-4
@@ -45,9 +50,10 @@ def test_tiny_matches_reference_golden(cuda, golden, tiny):
     eng.close()
 
 
-def test_graph_decode_equals_stepwise(cuda, tiny):
+@MODES
+def test_graph_decode_equals_stepwise(cuda, tiny, mode):
     cfg = G.QWEN3_TINY
-    eng = B.Engine(cfg, kv_capacity=128, max_batch=32).load_gguf(tiny).finalize()
+    eng = B.Engine(cfg, kv_capacity=128, max_batch=32, decode_mode=mode).load_gguf(tiny).finalize()
     prompt = np.arange(20, dtype=np.int32) * 13 % cfg.n_vocab
     t0 = eng.eval(prompt)
     stepwise = [t0]
@@ -58,6 +64,32 @@ def test_graph_decode_equals_stepwise(cuda, tiny):
     gen = eng.generate(30)  # on-device loop, tokens fed back without the host
     assert list(gen) == stepwise[1:]
     assert eng.n_past == 50
+    tr = eng.trace().astype(np.int64)  # one traced step leaves the state unchanged
+    assert tr.shape[0] == 5 * cfg.n_layer + 1 and eng.n_past == 50
+    assert np.all(tr[:, 3] > 0) and np.all(np.diff(tr[:, 3]) >= 0)
+    eng.close()
+
+
+@MODES
+def test_long_context_decode(cuda, port, tiny, mode):
+    """Decode at positions 700..707 (18 attention splits per KV head, the maximum, in the single-launch
+    kernel) against the restatement, logits within 1e-4 of the logit scale."""
+    cfg = G.QWEN3_TINY
+    rd = G.GGUFReader(tiny)
+    pm = oracle.PortQwen3(port, cfg.as_dict(), {n: np.array(rd.tensor(n)) for n in rd.names()}, kv_capacity=720)
+    eng = B.Engine(cfg, kv_capacity=720, max_batch=512, decode_mode=mode).load_gguf(tiny).finalize()
+    prompt = np.random.default_rng(3).integers(0, cfg.n_vocab, 700).astype(np.int32)
+    lg = np.empty(cfg.n_vocab, np.float32)
+    for chunk in (prompt[:400], prompt[400:]):
+        eng.eval(chunk)
+        want = pm.eval(chunk, threads=THREADS)[0]
+    tok = port.argmax(want)
+    for _ in range(8):
+        got = eng.eval(np.array([tok], np.int32), lg)
+        want = pm.eval(np.array([tok], np.int32), threads=THREADS)[0]
+        assert rel_err(lg, want) <= 1e-4
+        tok = port.argmax(want)
+        assert got == tok
     eng.close()
 
 
@@ -104,8 +136,9 @@ def test_missing_weights_rejected(cuda):
     eng.close()
 
 
+@MODES
 @pytest.mark.parametrize("steps", [16])
-def test_qwen3_06b_teacher_forced(cuda, port, steps):
+def test_qwen3_06b_teacher_forced(cuda, port, steps, mode):
     """Qwen3-0.6B shape, 32-token prompt: greedy tokens agree with the restatement at
     every teacher-forced step and logits stay within 1e-4 of the logit scale."""
     cfg = G.QWEN3_0_6B
@@ -113,7 +146,8 @@ def test_qwen3_06b_teacher_forced(cuda, port, steps):
     rd = G.GGUFReader(path)
     weights = {n: rd.tensor(n) for n in rd.names()}
     pm = oracle.PortQwen3(port, cfg.as_dict(), weights, kv_capacity=64)
-    eng = B.Engine(cfg, kv_capacity=64, max_batch=32).load_gguf(path).finalize()
+    eng = B.Engine(cfg, kv_capacity=64, max_batch=32, decode_mode=mode).load_gguf(path).finalize()
+    assert eng.decode_launches == (1 if mode == B.DECODE_SINGLE else 5 * cfg.n_layer + 1)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, cfg.n_vocab, 32).astype(np.int32)
     lg = np.empty(cfg.n_vocab, np.float32)
