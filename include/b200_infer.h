@@ -181,9 +181,9 @@ typedef struct b200_qwen3_config {
     int32_t precision;     /* B200_PREC_* for prefill matrix products */
     /* tensor parallelism (1 = single GPU); rank/world index this process */
     int32_t tp_rank, tp_world;
-    /* decode step: B200_DECODE_AUTO (the faster of the two for this shape),
-     * B200_DECODE_MULTI (the multi-kernel chain) or B200_DECODE_SINGLE (the
-     * persistent single-launch kernel where the shape allows it, else multi) */
+    /* decode step: B200_DECODE_AUTO or B200_DECODE_SINGLE (the persistent
+     * single-launch kernel where the shape allows it on one GPU, else the
+     * multi-kernel chain) or B200_DECODE_MULTI (always the multi-kernel chain) */
     int32_t decode_mode;
 } b200_qwen3_config;
 

@@ -106,6 +106,21 @@ B200_DEVICE bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep up to `sleep_ns` in hardware until the
+// phase completes instead of returning at once: a waiting warp takes no issue slots
+// from the warps that share its scheduler.
+B200_DEVICE bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t sleep_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(sleep_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (after B200_SPIN_LIMIT polls) if it never does.
 B200_DEVICE bool mbar_wait(uint64_t *bar, uint32_t parity) {

@@ -1,18 +1,20 @@
 // Persistent decode megakernel: one cooperative launch runs a whole decode step
 // (28 layers x [QKV, attention, o_proj, gate/up, down] + LM head + greedy argmax)
-// with one CTA of 8 warps per SM.
+// with one CTA per SM: 8 consumer warps and a producer warpgroup.
 //
 // Weight streaming is decoupled from the activation dependency chain. The step's
 // static weight schedule (this CTA's row slice of every projection, layer after
-// layer, then the LM head) is cut into ring chunks of whole rows; chunk c belongs
-// to warp c % 8 and lives in shared-memory slot c % 16, so every warp refills its
-// own two slots with cp.async.bulk (TMA engine, mbarrier completion) the moment
-// it has read them. Copies therefore run 16 chunks (192 KB) ahead of consumption
-// and L2 bulk prefetches a further prefetch_chunks ahead, across phase boundaries
-// and grid barriers, so HBM keeps streaming while the CTA waits on activations.
-// Phases are separated by grid barriers (an L2 counter, bounded polling); each
-// phase reads its input activation through L2 (ld.global.cg), consumes its chunks
-// (one warp per chunk, several chunks in flight) and writes its outputs.
+// layer, then the LM head) is cut into ring chunks of whole rows; a producer
+// thread streams them through a 16-slot shared-memory ring with cp.async.bulk
+// (TMA engine, mbarrier completion) and keeps L2 bulk prefetches further ahead,
+// so HBM keeps streaming while the consumers wait on activations. Chunk c is
+// read by consumer warp c % 8 from slot c % 16.
+//
+// There are no grid barriers. Every activation a CTA hands to others (q/k/v rows,
+// attention split partials, residual rows, SwiGLU rows) is written as a tagged
+// 64-bit word (phase tag | float); the next phase's readers poll exactly the
+// words they need until the tag of that phase shows, which costs one store and
+// one load round trip instead of a release, a counter update and a poll.
 //
 // Numerics match the multi-kernel path up to summation order: RMSNorm in double
 // with the reference's rounding, row sums and split partials combined in a fixed
@@ -22,7 +24,6 @@
 
 #include "decode_mk.cuh"
 #include "gemv.cuh"
-#include "rope.cuh"
 
 namespace b200 {
 namespace {
@@ -129,20 +130,34 @@ struct Cursor {
     B200_DEVICE const float *src() const { return pw.w + (r0 + static_cast<int64_t>(k) * rpc) * pw.K; }
 };
 
-B200_DEVICE unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// L2-resident data on the critical path. The weight stream is read with an
+// evict_first policy; the KV cache, the norm weights and the RoPE table are read
+// and written with evict_last so that they stay in L2 from step to step instead of
+// queueing behind the stream in HBM.
+B200_DEVICE float4 ld_keep4(const float *p, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
     return v;
 }
-
+B200_DEVICE float2 ld_keep2(const float *p, uint64_t pol) {
+    float2 v;
+    asm volatile("ld.global.cg.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;" : "=f"(v.x), "=f"(v.y) : "l"(p), "l"(pol));
+    return v;
+}
+B200_DEVICE void st_keep(float *p, float v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
+}
+// E consecutive floats (E = 2 or 4, 8- or 16-byte aligned) with the keep policy.
 template <int E>
-B200_DEVICE void ldcg_vec(const float *src, float (&v)[E]) {
+B200_DEVICE void ld_keep_vec(const float *src, float (&v)[E], uint64_t pol) {
     if constexpr (E == 4) {
-        const float4 t = __ldcg(reinterpret_cast<const float4 *>(src));
+        const float4 t = ld_keep4(src, pol);
         v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
     } else {
         static_assert(E == 2, "head_dim 64 or 128");
-        const float2 t = __ldcg(reinterpret_cast<const float2 *>(src));
+        const float2 t = ld_keep2(src, pol);
         v[0] = t.x, v[1] = t.y;
     }
 }
@@ -154,18 +169,77 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s
 // Bounded wait on an mbarrier phase: abandoned as soon as any CTA has reported an
 // error (its peers may have stopped), and after kWaitNs (sets the timeout status).
 // status == nullptr: wait for this CTA's own copies in flight, ignoring errors.
+// The waiting thread sleeps in hardware between polls (woken when the phase
+// completes), so it does not steal issue slots from the warps beside it.
 B200_DEVICE bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
-    uint64_t t0 = 0;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
     for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 63) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 7) == 7) {
             if (status && status_set(status)) return false;
-            const uint64_t t = global_ns();
-            if (!t0) t0 = t;
-            else if (t - t0 > kWaitNs) break;
+            if (global_ns() - t0 > kWaitNs) break;
         }
     }
     if (status) set_status(status, B200_DEV_TIMEOUT);
+    return false;
+}
+
+// ---------------------------------------------------------------------------
+// Tagged activation words. Every value one CTA hands to others is stored as one
+// 64-bit word (tag << 32 | float bits) with a single relaxed gpu-scope store, so
+// a reader that sees the tag it expects also sees the value of that phase: no
+// fence, no flag, no grid barrier. Tags are (launch + 1) * kTagStride + phase
+// index, unique per launch (the launch counter advances on every launch, aborted
+// ones included), so nothing left over from an earlier step ever matches.
+// A buffer is rewritten only two phases after it was read, and every phase needs
+// the previous phase's outputs of all CTAs, so no writer can overtake a reader.
+constexpr uint32_t kTagStride = 256;  // > 5 * kMaxLayers + 1 phase indices
+using u64 = unsigned long long;
+
+B200_DEVICE uint32_t tag_hi(u64 w) { return static_cast<uint32_t>(w >> 32); }
+B200_DEVICE float tag_val(u64 w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+B200_DEVICE void st_tagged(u64 *p, float v, uint32_t tag) {
+    const u64 w = (static_cast<u64>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+B200_DEVICE void ld_tagged2(const u64 *p, u64 &a, u64 &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+B200_DEVICE u64 ld_tagged1(const u64 *p) {
+    u64 a;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+    return a;
+}
+
+// Polls word pairs until both carry `tag`: `pending` is a bit mask over the
+// caller's pairs, `reload(j)` re-reads pair j. Gives up (status set) after
+// kWaitNs or as soon as another CTA reported an error.
+template <int N, class Check, class Reload>
+B200_DEVICE bool poll_pairs(unsigned pending, const int32_t *status_p, int32_t *status, Check ok, Reload reload) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0; it < B200_SPIN_LIMIT; ++it) {
+        unsigned still = 0;
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (((pending >> j) & 1u) && !ok(j)) still |= 1u << j;
+        if (!still) return true;
+        if ((it & 15) == 15) {
+            if (status_set(status_p)) return false;
+            const uint64_t t = global_ns();
+            if (!t0) t0 = t;
+            else if (t - t0 > kWaitNs) {
+                set_status(status, B200_DEV_TIMEOUT);
+                return false;
+            }
+        }
+        __nanosleep(64);
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if ((still >> j) & 1u) reload(j);
+        pending = still;
+    }
+    set_status(status, B200_DEV_TIMEOUT);
     return false;
 }
 
@@ -184,72 +258,53 @@ struct Mk {
     const MkParams &p;
     const Smem &sm;
     const int tid, warp, lane, b, G;
+    const uint32_t tag0;                        // this launch's tag base
+    const uint64_t keep = policy_evict_last();  // KV cache, norm weights, RoPE table
 
-    // ---- grid barrier over the consumer threads of every CTA (bounded polling).
-    B200_DEVICE bool grid_sync(unsigned &epoch) {
-        __shared__ int s_ok;
-        named_sync(1, kCT);
-        epoch += static_cast<unsigned>(G);
-        if (tid == 0) {
-            // release at gpu scope is cumulative: it orders every consumer thread's
-            // phase outputs (ordered before it by the CTA barrier above)
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-            bool ok = false, failed = false;
-            uint64_t t0 = 0;
-            for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
-                if (ld_acquire(p.bar) >= epoch) {
-                    ok = true;
-                    break;
-                }
-                if (status_set(p.status)) {  // another CTA gave up
-                    failed = true;
-                    break;
-                }
-                if ((i & 15) == 15) {
-                    const uint64_t t = global_ns();
-                    if (!t0) t0 = t;
-                    else if (t - t0 > kWaitNs) break;
-                }
-            }
-            if (!ok && !failed) set_status(p.status, B200_DEV_TIMEOUT);
-            s_ok = ok;
-        }
-        named_sync(1, kCT);
-        return s_ok != 0;
-    }
+    B200_DEVICE uint32_t tag(int layer, int ph) const { return tag0 + static_cast<uint32_t>(layer * PH_PER_LAYER + ph); }
 
-    // ---- phase input: xs = src (optionally RMS-normalised with gamma), via L2.
-    // x and gamma loads are issued together (one L2 round trip), the sum of
-    // squares is reduced with a single CTA barrier.
-    B200_DEVICE void load_act(const float *src, int64_t K, const float *gamma, float *also_store) {
-        constexpr int kV = kMaxK / 4 / kCT;  // float4 per thread at most
+    // ---- phase input from tagged words: xs = src (optionally RMS-normalised with
+    // gamma), in rounds of kP word pairs per thread (all loads of a round in
+    // flight together, only stale pairs re-read); gamma is applied from shared
+    // memory once the sum of squares is known.
+    B200_DEVICE bool load_act(const u64 *src, int64_t K, const float *gamma, uint32_t want) {
+        constexpr int kP = 2;  // word pairs per thread per round (register budget)
         __shared__ double s_red[kCW];
-        const int64_t K4 = K >> 2;
-        const float4 *s4 = reinterpret_cast<const float4 *>(src);
-        const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
-        float4 v[kV], g[kV];
+        __shared__ int s_bad;
+        if (tid == 0) s_bad = 0;
+        const int64_t K2 = K >> 1;
+        float2 gv[kP];  // gamma of the first round, loaded with it
 #pragma unroll
-        for (int j = 0; j < kV; ++j) {
-            const int64_t i = tid + j * kCT;
-            if (i < K4) {
-                v[j] = __ldcg(s4 + i);
-                if (gamma) g[j] = __ldg(g4 + i);
-            }
-        }
+        for (int j = 0; j < kP; ++j)
+            if (gamma && tid + j * kCT < K2) gv[j] = ld_keep2(gamma + 2 * (tid + j * kCT), keep);
         double ss = 0.0;
+        bool ok = true;
+        for (int64_t base = 0; base < K2 && ok; base += kP * kCT) {
+            u64 a[kP], c[kP];
+            unsigned pending = 0;
 #pragma unroll
-        for (int j = 0; j < kV; ++j) {
-            const int64_t i = tid + j * kCT;
-            if (i < K4) {
-                if (also_store) reinterpret_cast<float4 *>(also_store)[i] = v[j];
-                const float q0 = v[j].x * v[j].x, q1 = v[j].y * v[j].y, q2 = v[j].z * v[j].z, q3 = v[j].w * v[j].w;
-                ss += static_cast<double>(q0);
-                ss += static_cast<double>(q1);
-                ss += static_cast<double>(q2);
-                ss += static_cast<double>(q3);
+            for (int j = 0; j < kP; ++j) {
+                const int64_t i = base + tid + j * kCT;
+                if (i < K2) {
+                    ld_tagged2(src + 2 * i, a[j], c[j]);
+                    pending |= 1u << j;
+                }
+            }
+            ok = poll_pairs<kP>(
+                pending, p.status, p.status, [&](int j) { return tag_hi(a[j]) == want && tag_hi(c[j]) == want; },
+                [&](int j) { ld_tagged2(src + 2 * (base + tid + j * kCT), a[j], c[j]); });
+#pragma unroll
+            for (int j = 0; j < kP; ++j) {
+                if ((pending >> j) & 1u) {
+                    const float x0 = tag_val(a[j]), x1 = tag_val(c[j]);
+                    const float q0 = x0 * x0, q1 = x1 * x1;
+                    ss += static_cast<double>(q0);
+                    ss += static_cast<double>(q1);
+                    reinterpret_cast<float2 *>(sm.xs)[base + tid + j * kCT] = make_float2(x0, x1);
+                }
             }
         }
-        float sc = 1.f;
+        if (!ok) s_bad = 1;
         if (gamma) {
             ss = warp_sum(ss);
             if (lane == 0) s_red[warp] = ss;
@@ -257,19 +312,63 @@ struct Mk {
             double t = 0.0;  // every thread sums the warp totals in the same order
 #pragma unroll
             for (int w = 0; w < kCW; ++w) t += s_red[w];
-            sc = rms_scale_from_sumsq(t, K, p.eps);
+            const float sc = rms_scale_from_sumsq(t, K, p.eps);
+            auto apply = [&](int64_t i, float2 g) {  // only pairs this thread wrote
+                float2 y = reinterpret_cast<float2 *>(sm.xs)[i];
+                y.x = __fmul_rn(__fmul_rn(y.x, sc), g.x);
+                y.y = __fmul_rn(__fmul_rn(y.y, sc), g.y);
+                reinterpret_cast<float2 *>(sm.xs)[i] = y;
+            };
+#pragma unroll
+            for (int j = 0; j < kP; ++j)
+                if (tid + j * kCT < K2) apply(tid + j * kCT, gv[j]);
+            for (int64_t i = tid + kP * kCT; i < K2; i += kCT) apply(i, ld_keep2(gamma + 2 * i, keep));
         }
+        named_sync(1, kCT);
+        return s_bad == 0;  // uniform over the CTA
+    }
+
+    // ---- the same from plain floats (the token's embedding row).
+    B200_DEVICE void load_act_plain(const float *src, int64_t K, const float *gamma) {
+        constexpr int kV = kMaxK / 4 / kCT;
+        __shared__ double s_red[kCW];
+        const int64_t K4 = K >> 2;
+        float4 v[kV], g[kV];
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int64_t i = tid + j * kCT;
+            if (i < K4) {
+                v[j] = __ldg(reinterpret_cast<const float4 *>(src) + i);
+                g[j] = ld_keep4(gamma + 4 * i, keep);
+            }
+        }
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            if (tid + j * kCT < K4) {
+                const float q0 = v[j].x * v[j].x, q1 = v[j].y * v[j].y, q2 = v[j].z * v[j].z, q3 = v[j].w * v[j].w;
+                ss += static_cast<double>(q0);
+                ss += static_cast<double>(q1);
+                ss += static_cast<double>(q2);
+                ss += static_cast<double>(q3);
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_red[warp] = ss;
+        named_sync(1, kCT);
+        double t = 0.0;
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) t += s_red[w];
+        const float sc = rms_scale_from_sumsq(t, K, p.eps);
 #pragma unroll
         for (int j = 0; j < kV; ++j) {
             const int64_t i = tid + j * kCT;
             if (i < K4) {
                 float4 y = v[j];
-                if (gamma) {
-                    y.x = __fmul_rn(__fmul_rn(y.x, sc), g[j].x);
-                    y.y = __fmul_rn(__fmul_rn(y.y, sc), g[j].y);
-                    y.z = __fmul_rn(__fmul_rn(y.z, sc), g[j].z);
-                    y.w = __fmul_rn(__fmul_rn(y.w, sc), g[j].w);
-                }
+                y.x = __fmul_rn(__fmul_rn(y.x, sc), g[j].x);
+                y.y = __fmul_rn(__fmul_rn(y.y, sc), g[j].y);
+                y.z = __fmul_rn(__fmul_rn(y.z, sc), g[j].z);
+                y.w = __fmul_rn(__fmul_rn(y.w, sc), g[j].w);
                 reinterpret_cast<float4 *>(sm.xs)[i] = y;
             }
         }
@@ -386,18 +485,71 @@ struct Mk {
         return max(1, min(S, min(kMaxSplits, G / p.Hkv)));
     }
 
+    // One lane's E consecutive tagged words of a head (E even), waiting for `want`.
+    B200_DEVICE bool read_head_lane(const u64 *src, uint32_t want, float (&v)[E]) {
+        constexpr int NP = E / 2;
+        u64 a[NP], c[NP];
+#pragma unroll
+        for (int j = 0; j < NP; ++j) ld_tagged2(src + lane * E + 2 * j, a[j], c[j]);
+        const bool ok = poll_pairs<NP>(
+            (1u << NP) - 1, p.status, p.status, [&](int j) { return tag_hi(a[j]) == want && tag_hi(c[j]) == want; },
+            [&](int j) { ld_tagged2(src + lane * E + 2 * j, a[j], c[j]); });
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+            v[2 * j] = tag_val(a[j]);
+            v[2 * j + 1] = tag_val(c[j]);
+        }
+        return ok;
+    }
+
+    // One warp: RMSNorm + NeoX RoPE of one head of D = 32 E floats (reference
+    // rounding: float squares summed in double, y = (x * scale) * gamma, angle =
+    // float(double(pos) * freq_j), separately rounded rotation products). The head
+    // comes from tagged words; gamma and the frequency table are loaded with it.
+    B200_DEVICE bool norm_rope_head(const u64 *src, uint32_t want, const float *gamma, int64_t pos, float *dst) {
+        const bool lo = lane < 16;
+        float v[E], gm[E], fr[E];
+        ld_keep_vec(gamma + lane * E, gm, keep);
+        ld_keep_vec(p.freq + (lo ? lane : lane - 16) * E, fr, keep);
+        const bool ok = read_head_lane(src, want, v);
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const float sq = v[e] * v[e];
+            ss += static_cast<double>(sq);
+        }
+        ss = warp_sum(ss);
+        const float sc = rms_scale_from_sumsq(ss, D, p.eps);
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc), gm[e]);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            const float ang = static_cast<float>(static_cast<double>(pos) * static_cast<double>(fr[e]));
+            float s, c;
+            sincosf(ang, &s, &c);
+            dst[lane * E + e] = lo ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s))
+                                   : __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
+        }
+        return __all_sync(0xffffffffu, ok);
+    }
+
     // ---- attention for one (KV head, split): fused q/k norm + RoPE, KV append,
     // online softmax over the split's keys in batches of kTB. The first batch of
     // cached keys/values is in flight while the queries and the new token are
     // normalised; the new token's k/v come from shared memory (the cache row is
-    // written for later steps only), so there is no fence on the path.
-    B200_DEVICE void attention(int layer, int64_t n_past) {
+    // written for later steps only). Partials go out as tagged words.
+    B200_DEVICE bool attention(int layer, int64_t n_past) {
         constexpr int kTB = 8;
         const MkLayer &Lw = s_layers[layer];
+        const uint32_t want = tag(layer, PH_QKV), mine = tag(layer, PH_ATTN);
         const int Gq = p.Hq / p.Hkv;
         const int64_t L = n_past + 1;
         const int S = attn_splits(L);
-        if (b >= p.Hkv * S) return;
+        if (b >= p.Hkv * S) return true;
+        __shared__ int s_bad;
+        if (tid == 0) s_bad = 0;
+        named_sync(1, kCT);  // sm.part (new k/v) is free: the QKV epilogue has read it
         const int g = b / S, s = b % S;
         const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
         const bool last = (s == S - 1);
@@ -412,8 +564,8 @@ struct Mk {
 #pragma unroll
             for (int j = 0; j < kTB; ++j) {
                 if (j < n && t + j != n_past) {
-                    ldcg_vec(kb + (t + j) * tok, kv[j]);
-                    ldcg_vec(vb + (t + j) * tok, vv[j]);
+                    ld_keep_vec(kb + (t + j) * tok, kv[j], keep);
+                    ld_keep_vec(vb + (t + j) * tok, vv[j], keep);
                 } else {
 #pragma unroll
                     for (int e = 0; e < E; ++e) kv[j][e] = vv[j][e] = 0.f;
@@ -421,22 +573,26 @@ struct Mk {
             }
         };
         load_batch(t0, static_cast<int>(min64(kTB, t1 - t0)));
+        bool ok = true;
         if (last && warp == 0) {  // new token k: normalised + rotated
-            warp_norm_rope_head<E, true>(p.qkv + (p.Hq + g) * D, Lw.k_norm, p.freq, n_past, p.eps, kn);
+            ok = norm_rope_head(p.tqkv + (p.Hq + g) * D, want, Lw.k_norm, n_past, kn);
             __syncwarp();
             float *dst = Lw.kc + n_past * tok + g * D;
-            for (int d = lane; d < D; d += 32) dst[d] = kn[d];
+            for (int d = lane; d < D; d += 32) st_keep(dst + d, kn[d], keep);
         } else if (last && warp == 1) {  // new token v as is
-            const float *vsrc = p.qkv + (p.Hq + p.Hkv + g) * D;
+            float v[E];
+            ok = __all_sync(0xffffffffu, read_head_lane(p.tqkv + (p.Hq + p.Hkv + g) * D, want, v));
             float *vdst = Lw.vc + n_past * tok + g * D;
-            for (int d = lane; d < D; d += 32) {
-                const float v = __ldcg(vsrc + d);
-                vn[d] = v;
-                vdst[d] = v;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                vn[lane * E + e] = v[e];
+                st_keep(vdst + lane * E + e, v[e], keep);
             }
         }
-        warp_norm_rope_head<E, true>(p.qkv + h * D, Lw.q_norm, p.freq, n_past, p.eps, sm.qs + warp * D);
+        ok = norm_rope_head(p.tqkv + h * D, want, Lw.q_norm, n_past, sm.qs + warp * D) && ok;
+        if (!ok && lane == 0) s_bad = 1;
         named_sync(1, kCT);
+        if (s_bad) return false;
         float q[E];
 #pragma unroll
         for (int e = 0; e < E; ++e) q[e] = sm.qs[warp * D + lane * E + e];
@@ -500,7 +656,7 @@ struct Mk {
             wp[D + 1] = l;
         }
         named_sync(1, kCT);
-        // combine the token sub-ranges of each head in order -> split partial in L2
+        // combine the token sub-ranges of each head in order -> the split's partial
         for (int i = tid; i < Gq * D; i += kCT) {
             const int hh = i / D, d = i % D;
             float M = -INFINITY;
@@ -514,47 +670,57 @@ struct Mk {
                 os = fmaf(f, w[d], os);
             }
             const int64_t sh = static_cast<int64_t>(s) * p.Hq + g * Gq + hh;
-            p.attn_part[sh * D + d] = os;
+            st_tagged(p.tpo + sh * D + d, os, mine);
             if (d == 0) {
-                float *ml = p.attn_part + static_cast<int64_t>(kMaxSplits) * p.Hq * D + sh * 2;
-                ml[0] = M;
-                ml[1] = lsum;
+                st_tagged(p.tpml + sh * 2, M, mine);
+                st_tagged(p.tpml + sh * 2 + 1, lsum, mine);
             }
         }
+        return true;
     }
 
-    // ---- o_proj input: merge the attention splits (split order) into xs. The
-    // first kSG splits' partial outputs (float4 slices per thread) are in flight
-    // together with every split's (m, l): one L2 round trip up to kSG splits.
-    B200_DEVICE void merge_attention(int64_t n_past) {
-        constexpr int kV = kMaxK / 4 / kCT;  // float4 per thread at most
-        constexpr int kSG = 6;               // splits loaded per round
+    // ---- o_proj input: merge the attention splits (split order) into xs. Every
+    // split's (m, l) first, then per thread its word pairs of up to kSG splits'
+    // partial outputs in flight together.
+    B200_DEVICE bool merge_attention(int layer, int64_t n_past) {
+        constexpr int kP = 4;   // word pairs per thread: Hq * D <= 2 * kP * kCT
+        constexpr int kSG = 2;  // splits loaded per round (register budget)
+        const uint32_t want = tag(layer, PH_ATTN);
         const int S = attn_splits(n_past + 1);
         const int Hq = p.Hq;
-        const float *ml = p.attn_part + static_cast<int64_t>(kMaxSplits) * Hq * D;
-        const int n4 = Hq * D / 4;
-        const float4 *o4 = reinterpret_cast<const float4 *>(p.attn_part);
-        float4 ov[kSG][kV];
-        auto load_group = [&](int s0) {
-#pragma unroll
-            for (int j = 0; j < kSG; ++j)
-#pragma unroll
-                for (int v = 0; v < kV; ++v) {
-                    const int i4 = tid + v * kCT;
-                    ov[j][v] = (s0 + j < S && i4 < n4) ? __ldcg(o4 + static_cast<int64_t>(s0 + j) * n4 + i4)
-                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-        };
-        load_group(0);
+        const int n2 = Hq * D / 2;
         float *sw = sm.part;                      // [S][Hq]: m, then the split weight
         float *sl = sm.part + kMaxSplits * Hq;    // [S][Hq]: l
         float *sden = sl + kMaxSplits * Hq;       // [Hq]: sum of weighted l
-        for (int i = tid; i < S * Hq; i += kCT) {
-            const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
-            sw[i] = v.x;
-            sl[i] = v.y;
-        }
+        __shared__ int s_bad;
+        if (tid == 0) s_bad = 0;
         named_sync(1, kCT);
+        bool ok = true;
+        {
+            constexpr int kM = 2;  // (split, head) pairs per thread: kMaxSplits * Hq <= kM * kCT
+            u64 a[kM], c[kM];
+            unsigned pending = 0;
+#pragma unroll
+            for (int j = 0; j < kM; ++j) {
+                const int i = tid + j * kCT;
+                if (i < S * Hq) {
+                    ld_tagged2(p.tpml + 2 * i, a[j], c[j]);
+                    pending |= 1u << j;
+                }
+            }
+            ok = poll_pairs<kM>(
+                pending, p.status, p.status, [&](int j) { return tag_hi(a[j]) == want && tag_hi(c[j]) == want; },
+                [&](int j) { ld_tagged2(p.tpml + 2 * (tid + j * kCT), a[j], c[j]); });
+#pragma unroll
+            for (int j = 0; j < kM; ++j)
+                if ((pending >> j) & 1u) {
+                    sw[tid + j * kCT] = tag_val(a[j]);
+                    sl[tid + j * kCT] = tag_val(c[j]);
+                }
+        }
+        if (!ok) s_bad = 1;
+        named_sync(1, kCT);
+        if (s_bad) return false;
         for (int hh = tid; hh < Hq; hh += kCT) {
             float M = -INFINITY;
             for (int s = 0; s < S; ++s) M = fmaxf(M, sw[s * Hq + hh]);
@@ -568,35 +734,52 @@ struct Mk {
             sden[hh] = lsum;
         }
         named_sync(1, kCT);
-        float4 acc[kV];
+        float2 acc[kP];
 #pragma unroll
-        for (int v = 0; v < kV; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s0 = 0; s0 < S; s0 += kSG) {
-            if (s0) load_group(s0);
+        for (int v = 0; v < kP; ++v) acc[v] = make_float2(0.f, 0.f);
+        for (int s0 = 0; s0 < S && ok; s0 += kSG) {
+            u64 a[kSG * kP], c[kSG * kP];
+            unsigned pending = 0;
 #pragma unroll
             for (int j = 0; j < kSG; ++j)
 #pragma unroll
-                for (int v = 0; v < kV; ++v) {
-                    const int i4 = tid + v * kCT;
-                    if (s0 + j < S && i4 < n4) {
-                        const float f = sw[(s0 + j) * Hq + i4 * 4 / D];
-                        acc[v].x = fmaf(f, ov[j][v].x, acc[v].x);
-                        acc[v].y = fmaf(f, ov[j][v].y, acc[v].y);
-                        acc[v].z = fmaf(f, ov[j][v].z, acc[v].z);
-                        acc[v].w = fmaf(f, ov[j][v].w, acc[v].w);
+                for (int v = 0; v < kP; ++v) {
+                    const int i2 = tid + v * kCT;
+                    if (s0 + j < S && i2 < n2) {
+                        ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + i2) * 2, a[j * kP + v], c[j * kP + v]);
+                        pending |= 1u << (j * kP + v);
+                    }
+                }
+            ok = poll_pairs<kSG * kP>(
+                pending, p.status, p.status,
+                [&](int q) { return tag_hi(a[q]) == want && tag_hi(c[q]) == want; },
+                [&](int q) {
+                    const int j = q / kP, v = q % kP;
+                    ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + tid + v * kCT) * 2, a[q], c[q]);
+                });
+#pragma unroll
+            for (int j = 0; j < kSG; ++j)
+#pragma unroll
+                for (int v = 0; v < kP; ++v) {
+                    const int i2 = tid + v * kCT;
+                    if (s0 + j < S && i2 < n2) {
+                        const float f = sw[(s0 + j) * Hq + i2 * 2 / D];
+                        acc[v].x = fmaf(f, tag_val(a[j * kP + v]), acc[v].x);
+                        acc[v].y = fmaf(f, tag_val(c[j * kP + v]), acc[v].y);
                     }
                 }
         }
+        if (!ok) s_bad = 1;
 #pragma unroll
-        for (int v = 0; v < kV; ++v) {
-            const int i4 = tid + v * kCT;
-            if (i4 < n4) {
-                const float den = sden[i4 * 4 / D];
-                reinterpret_cast<float4 *>(sm.xs)[i4] =
-                    make_float4(acc[v].x / den, acc[v].y / den, acc[v].z / den, acc[v].w / den);
+        for (int v = 0; v < kP; ++v) {
+            const int i2 = tid + v * kCT;
+            if (i2 < n2) {
+                const float den = sden[i2 * 2 / D];
+                reinterpret_cast<float2 *>(sm.xs)[i2] = make_float2(acc[v].x / den, acc[v].y / den);
             }
         }
         named_sync(1, kCT);
+        return s_bad == 0;
     }
 };
 
@@ -611,8 +794,8 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p);
 // c % kStages for chunk c, refilled as soon as its consumer warp releases it) and
 // keeps L2 bulk prefetches prefetch_chunks ahead of the copies; past the LM head
 // the prefetches warm the head of the schedule for the next step (same weights).
-// It never waits on activations, so HBM keeps streaming while the consumers sit in
-// attention or at a grid barrier. Every wait is bounded and abandoned on error.
+// It never waits on activations, so HBM keeps streaming while the consumers wait
+// for other CTAs' outputs. Every wait is bounded and abandoned on error.
 B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
     const uint64_t pol = policy_evict_first();
     Cursor cp, pf;
@@ -653,6 +836,7 @@ B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ uint32_t s_tag0;
     Smem sm;
     sm.full = reinterpret_cast<uint64_t *>(smem_raw);
     sm.empty = sm.full + kStages;
@@ -665,6 +849,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x, G = gridDim.x;
     if (tid == 0) {
+        // every CTA of every launch takes one ticket: launch = ticket / G
+        const unsigned ticket = atomicAdd(p.launches, 1u);
+        s_tag0 = (ticket / static_cast<unsigned>(G) + 1u) * kTagStride;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);  // the one warp that reads the slot's chunk
@@ -686,17 +873,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
         return;
     }
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
-    Mk<D> mk{p, sm, tid, warp, lane, b, G};
+    Mk<D> mk{p, sm, tid, warp, lane, b, G, s_tag0};
     run_step<D>(mk, p);
 }
 
 template <int D>
 B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
     const int tid = mk.tid, warp = mk.warp, lane = mk.lane, b = mk.b, G = mk.G;
-    // The argmax ticket counter starts at zero even after an aborted step; every
-    // ticket is taken after the first grid barrier, which orders it after this.
-    if (b == 0 && tid == 0) *p.am_counter = 0u;
-    unsigned epoch = 0;
     int cc = 0;
     const int64_t n_past = *p.n_past;
     const int32_t token = *p.token;
@@ -705,79 +888,74 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
         if (tid == 0) set_status(p.status, B200_DEV_BAD_POSITION);
         ok = false;
     }
-    const bool bad_tok = token < 0 || token >= p.V;  // V == vocabulary on one GPU
-    if (bad_tok) {
+    if (token < 0 || token >= p.V) {  // V == vocabulary on one GPU
         if (tid == 0) set_status(p.status, B200_DEV_BAD_TOKEN);
         ok = false;
     }
+    const float *emb = p.tok_embd + static_cast<int64_t>(ok ? token : 0) * p.H;
     int64_t r0 = 0, r1 = 0;
     for (int l = 0; l < p.n_layer && ok; ++l) {
         const MkLayer &Lw = s_layers[l];
         const int base = l * PH_PER_LAYER;
-        // QKV (layer 0 reads the embedding row and stores it as the residual)
+        // QKV (layer 0 reads the token's embedding row)
         stamp(p, base + PH_QKV, 3);
         if (l == 0)
-            mk.load_act(p.tok_embd + static_cast<int64_t>(token) * p.H, p.H, Lw.attn_norm, b == 0 ? p.x : nullptr);
-        else
-            mk.load_act(p.x, p.H, Lw.attn_norm, nullptr);
+            mk.load_act_plain(emb, p.H, Lw.attn_norm);
+        else if (!mk.load_act(p.tx, p.H, Lw.attn_norm, mk.tag(l - 1, PH_DOWN)))
+            break;
         stamp(p, base + PH_QKV, 4);
         PhaseW pw = phase_w(p, l, PH_QKV);
         rows_of(pw.N, 1, b, G, r0, r1);
         ok = mk.consume(pw, r0, r1, cc, base + PH_QKV);
-        {
-            for (int64_t r = r0 + tid; r < r1; r += kCT) p.qkv[r] = mk.row_sum(r - r0);
-        }
+        for (int64_t r = r0 + tid; r < r1; r += kCT) st_tagged(p.tqkv + r, mk.row_sum(r - r0), mk.tag(l, PH_QKV));
         stamp(p, base + PH_QKV, 5);
-        if (!ok || !mk.grid_sync(epoch)) break;
         stamp(p, base + PH_QKV, 2);
+        if (!ok) break;
         // attention
         stamp(p, base + PH_ATTN, 3);
-        mk.attention(l, n_past);
+        ok = mk.attention(l, n_past);
         stamp(p, base + PH_ATTN, 5);
-        if (!mk.grid_sync(epoch)) break;
         stamp(p, base + PH_ATTN, 2);
-        // o_proj + residual
+        if (!ok) break;
+        // o_proj + residual (the residual rows are this CTA's own earlier writes)
         stamp(p, base + PH_O, 3);
-        mk.merge_attention(n_past);
+        if (!mk.merge_attention(l, n_past)) break;
         stamp(p, base + PH_O, 4);
         pw = phase_w(p, l, PH_O);
         rows_of(pw.N, 1, b, G, r0, r1);
         ok = mk.consume(pw, r0, r1, cc, base + PH_O);
-        {
-            for (int64_t r = r0 + tid; r < r1; r += kCT) p.x[r] = mk.row_sum(r - r0) + __ldcg(p.x + r);
+        for (int64_t r = r0 + tid; r < r1; r += kCT) {
+            const float prev = l == 0 ? __ldg(emb + r) : tag_val(ld_tagged1(p.tx + r));
+            st_tagged(p.tx + r, mk.row_sum(r - r0) + prev, mk.tag(l, PH_O));
         }
         stamp(p, base + PH_O, 5);
-        if (!ok || !mk.grid_sync(epoch)) break;
         stamp(p, base + PH_O, 2);
+        if (!ok) break;
         // gate/up + SwiGLU
         stamp(p, base + PH_GU, 3);
-        mk.load_act(p.x, p.H, Lw.ffn_norm, nullptr);
+        if (!mk.load_act(p.tx, p.H, Lw.ffn_norm, mk.tag(l, PH_O))) break;
         stamp(p, base + PH_GU, 4);
         pw = phase_w(p, l, PH_GU);
         rows_of(pw.N, 2, b, G, r0, r1);
         ok = mk.consume(pw, r0, r1, cc, base + PH_GU);
-        {
-            for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
-                const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
-                const float sg = gt / (1.0f + expf(-gt));
-                p.h[pr] = up * sg;
-            }
+        for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
+            const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
+            const float sg = gt / (1.0f + expf(-gt));
+            st_tagged(p.th + pr, up * sg, mk.tag(l, PH_GU));
         }
         stamp(p, base + PH_GU, 5);
-        if (!ok || !mk.grid_sync(epoch)) break;
         stamp(p, base + PH_GU, 2);
+        if (!ok) break;
         // down + residual
         stamp(p, base + PH_DOWN, 3);
-        mk.load_act(p.h, p.F, nullptr, nullptr);
+        if (!mk.load_act(p.th, p.F, nullptr, mk.tag(l, PH_GU))) break;
         stamp(p, base + PH_DOWN, 4);
         pw = phase_w(p, l, PH_DOWN);
         rows_of(pw.N, 1, b, G, r0, r1);
         ok = mk.consume(pw, r0, r1, cc, base + PH_DOWN);
-        {
-            for (int64_t r = r0 + tid; r < r1; r += kCT) p.x[r] = mk.row_sum(r - r0) + __ldcg(p.x + r);
-        }
+        for (int64_t r = r0 + tid; r < r1; r += kCT)
+            st_tagged(p.tx + r, mk.row_sum(r - r0) + tag_val(ld_tagged1(p.tx + r)), mk.tag(l, PH_DOWN));
         stamp(p, base + PH_DOWN, 5);
-        if (!ok || !mk.grid_sync(epoch)) break;
         stamp(p, base + PH_DOWN, 2);
     }
     if (!ok || status_set(p.status)) return;
@@ -785,7 +963,7 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
     // ---- LM head + greedy argmax (first maximum; NaN / +inf -> -1)
     const int lm = p.n_layer * PH_PER_LAYER;
     stamp(p, lm, 3);
-    mk.load_act(p.x, p.H, p.out_norm, nullptr);
+    if (!mk.load_act(p.tx, p.H, p.out_norm, mk.tag(p.n_layer - 1, PH_DOWN))) return;
     stamp(p, lm, 4);
     const PhaseW pw = phase_w(p, p.n_layer, 0);
     rows_of(pw.N, 1, b, G, r0, r1);
@@ -893,9 +1071,8 @@ int mk_prefetch_chunks() {
     return v;
 }
 int mk_max_splits() { return kMaxSplits; }
-size_t mk_attn_part_floats(const MkParams &p) {
-    return static_cast<size_t>(kMaxSplits) * p.Hq * (p.D + 2);
-}
+size_t mk_po_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * p.D; }
+size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * 2; }
 
 bool mk_supported(const MkParams &p) {
     if (p.D != 64 && p.D != 128) return false;
@@ -903,7 +1080,9 @@ bool mk_supported(const MkParams &p) {
     if (p.Hkv <= 0 || p.Hq % p.Hkv || kCW % (p.Hq / p.Hkv)) return false;
     const int G = mk_grid();
     if (p.Hkv > G) return false;
-    if (2 * kMaxSplits * p.Hq + p.Hq > kPartFloats) return false;  // merge scratch
+    // merge: scratch in sm.part, (split, head) pairs and output pairs per thread
+    if (2 * kMaxSplits * p.Hq + p.Hq > kPartFloats || kMaxSplits * p.Hq > 2 * kCT || p.Hq * p.D > 8 * kCT)
+        return false;
     const int64_t Ks[] = {p.H, static_cast<int64_t>(p.Hq) * p.D, p.F};
     for (int64_t K : Ks)
         if (K > kMaxK || (K & 3) || K < 64) return false;
@@ -925,8 +1104,6 @@ cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
     void *kern = p.D == 64 ? reinterpret_cast<void *>(decode_mk_kernel<64>) : reinterpret_cast<void *>(decode_mk_kernel<128>);
     // Per device and cheap: the launch is recorded once into the decode graph.
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(p.bar, 0, sizeof(unsigned), stream);
     if (e != cudaSuccess) return e;
     MkParams args = p;
     args.prefetch_chunks = mk_prefetch_chunks();

@@ -17,17 +17,21 @@ struct MkParams {
     float eps = 0.f;
     int64_t n_ctx = 0;                 // KV capacity (positions must stay below)
     const float *tok_embd = nullptr, *out_norm = nullptr, *lm_head = nullptr, *freq = nullptr;
-    float *x = nullptr;                // residual [H]
-    float *qkv = nullptr;              // [(Hq + 2 Hkv) D]
-    float *attn_part = nullptr;        // [max_splits][Hq][D + 2] split partials (o, m, l)
-    float *h = nullptr;                // [F]
+    // Activations exchanged between CTAs, as tagged words: (phase tag << 32) | float
+    // bits, written with one 64-bit store each. A reader waits for the tag of the
+    // phase it needs instead of a grid barrier; tags are unique per launch.
+    unsigned long long *tx = nullptr;    // residual [H]
+    unsigned long long *tqkv = nullptr;  // [(Hq + 2 Hkv) D]
+    unsigned long long *th = nullptr;    // SwiGLU output [F]
+    unsigned long long *tpo = nullptr;   // attention split partial outputs [max_splits][Hq][D]
+    unsigned long long *tpml = nullptr;  // attention split (max, sum) [max_splits][Hq][2]
+    unsigned *launches = nullptr;        // + gridDim.x per launch: the tag base (zero at create)
     float *logits = nullptr;           // [V] or nullptr
     int32_t *token = nullptr;          // in: token of this step; out: greedy next token
     int32_t *n_past = nullptr;         // advanced by 1 at the end of the step
     int32_t *status = nullptr;
     int32_t *token_log = nullptr, *log_pos = nullptr;
     int32_t log_cap = 0;
-    unsigned *bar = nullptr;           // grid-barrier counter, zero at launch
     float *am_val = nullptr;           // [gridDim.x] per-CTA argmax partials
     int32_t *am_idx = nullptr;
     unsigned *am_counter = nullptr;    // zero at launch; the last CTA re-zeroes it
@@ -39,8 +43,10 @@ struct MkParams {
 // True if the megakernel supports this model shape on this device.
 bool mk_supported(const MkParams &p);
 int mk_max_splits();
-size_t mk_attn_part_floats(const MkParams &p);
-// Enqueues the zeroing of the barrier counter and the cooperative launch.
+// Words of the split-partial buffers tpo / tpml.
+size_t mk_po_words(const MkParams &p);
+size_t mk_pml_words(const MkParams &p);
+// Enqueues the cooperative launch.
 cudaError_t mk_launch(const MkParams &p, cudaStream_t stream);
 int mk_grid();
 // L2 prefetch distance of each CTA ahead of its ring copies, in ring chunks.

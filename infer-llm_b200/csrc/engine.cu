@@ -512,6 +512,8 @@ int check_status(b200_engine *e) {
     B200_TRY(cudaStreamSynchronize(e->stream));
     if (s == 0) return B200_OK;
     B200_TRY(cudaMemsetAsync(e->status, 0, 4, e->stream));
+    // an aborted step may leave argmax tickets behind
+    B200_TRY(cudaMemsetAsync(e->am_counter, 0, 4, e->stream));
     B200_TRY(cudaStreamSynchronize(e->stream));
     if (s == B200_DEV_BAD_LOGITS) return B200_ERR_NUMERIC;
     if (s == B200_DEV_TIMEOUT) return B200_ERR_TIMEOUT;
@@ -628,8 +630,12 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     MkParams shape;
     shape.Hq = e->Hq;
     shape.D = static_cast<int>(D);
-    const size_t o_apart = take(static_cast<int64_t>(mk_attn_part_floats(shape)));
-    const size_t o_mkbar = take(64);
+    // tagged activation words of the single-launch decode step (8 bytes each)
+    const size_t o_tx = take(2 * H), o_tqkv = take(2 * static_cast<int64_t>(e->qkv_rows));
+    const size_t o_th = take(2 * F);
+    const size_t o_tpo = take(2 * static_cast<int64_t>(mk_po_words(shape)));
+    const size_t o_tpml = take(2 * static_cast<int64_t>(mk_pml_words(shape)));
+    const size_t o_mkl_n = take(64);
     e->act_bytes = off;
 
     cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
@@ -683,8 +689,13 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->tp_pairs = af(o_pairs);
     e->trace_buf = reinterpret_cast<unsigned long long *>(e->act_arena + o_trace);
     e->mk_layers = reinterpret_cast<MkLayer *>(e->act_arena + o_mkl);
-    e->mk.attn_part = af(o_apart);
-    e->mk.bar = reinterpret_cast<unsigned *>(e->act_arena + o_mkbar);
+    auto aw = [&](size_t o) { return reinterpret_cast<unsigned long long *>(e->act_arena + o); };
+    e->mk.tx = aw(o_tx);
+    e->mk.tqkv = aw(o_tqkv);
+    e->mk.th = aw(o_th);
+    e->mk.tpo = aw(o_tpo);
+    e->mk.tpml = aw(o_tpml);
+    e->mk.launches = reinterpret_cast<unsigned *>(e->act_arena + o_mkl_n);
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
     std::vector<float> hf(D / 2);
@@ -863,9 +874,6 @@ int b200_engine_finalize(b200_engine *e) {
     p.out_norm = e->out_norm;
     p.lm_head = e->lm_head;
     p.freq = e->freq;
-    p.x = e->x;
-    p.qkv = e->qkv;
-    p.h = e->h;
     p.logits = e->logits;  // V floats per step, so eval() can return logits from the graph step
     p.token = e->token;
     p.n_past = e->n_past_dev;
@@ -877,9 +885,9 @@ int b200_engine_finalize(b200_engine *e) {
     p.am_idx = e->am_idx;
     p.am_counter = e->am_counter;
     p.layers = e->mk_layers;
-    // AUTO keeps the multi-kernel chain until the single-launch kernel is faster
-    // on the benchmark shape.
-    e->use_mk = e->c.decode_mode == B200_DECODE_SINGLE && e->c.tp_world == 1 && mk_supported(p) &&
+    // AUTO takes the single-launch kernel wherever it supports the shape (it is the
+    // faster of the two on one GPU); MULTI forces the multi-kernel chain.
+    e->use_mk = e->c.decode_mode != B200_DECODE_MULTI && e->c.tp_world == 1 && mk_supported(p) &&
                 mk_grid() <= e->am_slots;
     if (e->use_mk) {
         std::vector<MkLayer> tab(e->c.n_layer);
