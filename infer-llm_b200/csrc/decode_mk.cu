@@ -112,6 +112,7 @@ struct Cursor {
     // Moves n chunks on; false once past the LM head.
     B200_DEVICE bool advance(const MkParams &p, int b, int G, int n) {
         k += n;
+#pragma unroll 1
         while (k >= nch) {
             if (l == p.n_layer) return false;
             k -= nch;
@@ -174,6 +175,7 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s
 B200_DEVICE bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
+#pragma unroll 1
     for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if ((i & 7) == 7) {
@@ -218,6 +220,7 @@ B200_DEVICE u64 ld_tagged1(const u64 *p) {
 template <int N, class Check, class Reload>
 B200_DEVICE bool poll_pairs(unsigned pending, const int32_t *status_p, int32_t *status, Check ok, Reload reload) {
     uint64_t t0 = 0;
+#pragma unroll 1
     for (uint32_t it = 0; it < B200_SPIN_LIMIT; ++it) {
         unsigned still = 0;
 #pragma unroll
@@ -279,6 +282,7 @@ struct Mk {
             if (gamma && tid + j * kCT < K2) gv[j] = ld_keep2(gamma + 2 * (tid + j * kCT), keep);
         double ss = 0.0;
         bool ok = true;
+#pragma unroll 1
         for (int64_t base = 0; base < K2 && ok; base += kP * kCT) {
             u64 a[kP], c[kP];
             unsigned pending = 0;
@@ -322,6 +326,7 @@ struct Mk {
 #pragma unroll
             for (int j = 0; j < kP; ++j)
                 if (tid + j * kCT < K2) apply(tid + j * kCT, gv[j]);
+#pragma unroll 1
             for (int64_t i = tid + kP * kCT; i < K2; i += kCT) apply(i, ld_keep2(gamma + 2 * i, keep));
         }
         named_sync(1, kCT);
@@ -378,14 +383,15 @@ struct Mk {
     // ---- R rows of one ring chunk against x (both in shared memory): each lane
     // takes float4 columns lane, lane + 32, ...; U columns per row are loaded
     // together (U * (R + 1) shared loads in flight) and accumulated per component
-    // so no FMA waits on the previous one. Releases the stage, then reduces the R
-    // row sums across the warp (fixed order) into dst[0..R).
+    // so no FMA waits on the previous one; then reduces the R row sums across the
+    // warp (fixed order) into dst[0..R).
     template <int R>
-    B200_DEVICE void chunk_rows(const float4 *w4, const float4 *x4, int64_t K4, uint64_t *empty, float *dst) {
+    B200_DEVICE void chunk_rows(const float4 *w4, const float4 *x4, int64_t K4, float *dst) {
         constexpr int U = R == 1 ? 8 : (R <= 3 ? 4 : 2);
         float4 a[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) a[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
         for (int64_t i0 = lane; i0 < K4; i0 += 32 * U) {
             float4 xv[U], wv[R][U];
 #pragma unroll
@@ -405,8 +411,6 @@ struct Mk {
                     a[r].w = fmaf(wv[r][u].w, xv[u].w, a[r].w);
                 }
         }
-        __syncwarp();  // the stage is read: hand it back to the producer
-        if (lane == 0) mbar_arrive(empty);
         float acc[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = (a[r].x + a[r].y) + (a[r].z + a[r].w);
@@ -438,6 +442,7 @@ struct Mk {
         __shared__ int s_fail;
         if (tid == 0) s_fail = 0;
         named_sync(1, kCT);
+#pragma unroll 1
         for (int64_t k = ((warp - cc) % kCW + kCW) % kCW; k < nch; k += kCW) {
             const int c = cc + static_cast<int>(k);
             const int s = c % kStages;
@@ -451,16 +456,18 @@ struct Mk {
             const int rows = static_cast<int>(min64(rpc, r1 - row));
             const float4 *w4 = reinterpret_cast<const float4 *>(sm.ring + static_cast<size_t>(s) * kStageFloats);
             float *dst = sm.part + (row - r0);
-            switch (rows) {
-                case 1: chunk_rows<1>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 2: chunk_rows<2>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 3: chunk_rows<3>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 4: chunk_rows<4>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 5: chunk_rows<5>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 6: chunk_rows<6>(w4, x4, K4, &sm.empty[s], dst); break;
-                case 7: chunk_rows<7>(w4, x4, K4, &sm.empty[s], dst); break;
-                default: chunk_rows<8>(w4, x4, K4, &sm.empty[s], dst); break;
+#pragma unroll 1
+            for (int r = 0; r < rows; r += 3) {  // sub-chunks of at most 3 rows
+                const int n = min(3, rows - r);
+                if (n == 3)
+                    chunk_rows<3>(w4 + r * K4, x4, K4, dst + r);
+                else if (n == 2)
+                    chunk_rows<2>(w4 + r * K4, x4, K4, dst + r);
+                else
+                    chunk_rows<1>(w4 + r * K4, x4, K4, dst + r);
             }
+            __syncwarp();  // the stage is read: hand it back to the producer
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
         }
         cc += static_cast<int>(nch);
         if (tr && lane == 0) {
@@ -522,14 +529,17 @@ struct Mk {
         const float sc = rms_scale_from_sumsq(ss, D, p.eps);
 #pragma unroll
         for (int e = 0; e < E; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc), gm[e]);
+        float other[E];
 #pragma unroll
+        for (int e = 0; e < E; ++e) other[e] = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        // one copy of the accurate sincosf (its large-argument path is big)
+#pragma unroll 1
         for (int e = 0; e < E; ++e) {
-            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
             const float ang = static_cast<float>(static_cast<double>(pos) * static_cast<double>(fr[e]));
             float s, c;
             sincosf(ang, &s, &c);
-            dst[lane * E + e] = lo ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, s))
-                                   : __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[e], c));
+            dst[lane * E + e] = lo ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other[e], s))
+                                   : __fadd_rn(__fmul_rn(other[e], s), __fmul_rn(v[e], c));
         }
         return __all_sync(0xffffffffu, ok);
     }
@@ -574,12 +584,21 @@ struct Mk {
         };
         load_batch(t0, static_cast<int>(min64(kTB, t1 - t0)));
         bool ok = true;
-        if (last && warp == 0) {  // new token k: normalised + rotated
-            ok = norm_rope_head(p.tqkv + (p.Hq + g) * D, want, Lw.k_norm, n_past, kn);
-            __syncwarp();
-            float *dst = Lw.kc + n_past * tok + g * D;
-            for (int d = lane; d < D; d += 32) st_keep(dst + d, kn[d], keep);
-        } else if (last && warp == 1) {  // new token v as is
+        // queries (every warp, its head) and, in warp 0 of the last split, the new
+        // token's key: one call site for the norm + RoPE code
+#pragma unroll 1
+        for (int pass = (last && warp == 0) ? 0 : 1; pass < 2; ++pass) {
+            const bool key = pass == 0;
+            ok = norm_rope_head(p.tqkv + (key ? p.Hq + g : h) * D, want, key ? Lw.k_norm : Lw.q_norm, n_past,
+                                key ? kn : sm.qs + warp * D) && ok;
+            if (key) {
+                __syncwarp();
+                float *dst = Lw.kc + n_past * tok + g * D;
+#pragma unroll 1
+                for (int d = lane; d < D; d += 32) st_keep(dst + d, kn[d], keep);
+            }
+        }
+        if (last && warp == 1) {  // new token v as is
             float v[E];
             ok = __all_sync(0xffffffffu, read_head_lane(p.tqkv + (p.Hq + p.Hkv + g) * D, want, v));
             float *vdst = Lw.vc + n_past * tok + g * D;
@@ -589,7 +608,6 @@ struct Mk {
                 st_keep(vdst + lane * E + e, v[e], keep);
             }
         }
-        ok = norm_rope_head(p.tqkv + h * D, want, Lw.q_norm, n_past, sm.qs + warp * D) && ok;
         if (!ok && lane == 0) s_bad = 1;
         named_sync(1, kCT);
         if (s_bad) return false;
@@ -600,6 +618,7 @@ struct Mk {
         float m = -INFINITY, l = 0.f, o[E];
 #pragma unroll
         for (int e = 0; e < E; ++e) o[e] = 0.f;
+#pragma unroll 1
         for (int64_t t = t0; t < t1; t += kTB) {
             const int n = static_cast<int>(min64(kTB, t1 - t));
             if (t != t0) load_batch(t, n);
@@ -657,11 +676,14 @@ struct Mk {
         }
         named_sync(1, kCT);
         // combine the token sub-ranges of each head in order -> the split's partial
+#pragma unroll 1
         for (int i = tid; i < Gq * D; i += kCT) {
             const int hh = i / D, d = i % D;
             float M = -INFINITY;
+#pragma unroll 1
             for (int u = 0; u < nsub; ++u) M = fmaxf(M, sm.wpart[(u * Gq + hh) * (D + 2) + D]);
             float lsum = 0.f, os = 0.f;
+#pragma unroll 1
             for (int u = 0; u < nsub; ++u) {
                 const float *w = sm.wpart + (u * Gq + hh) * (D + 2);
                 if (w[D] == -INFINITY) continue;
@@ -721,10 +743,13 @@ struct Mk {
         if (!ok) s_bad = 1;
         named_sync(1, kCT);
         if (s_bad) return false;
+#pragma unroll 1
         for (int hh = tid; hh < Hq; hh += kCT) {
             float M = -INFINITY;
+#pragma unroll 1
             for (int s = 0; s < S; ++s) M = fmaxf(M, sw[s * Hq + hh]);
             float lsum = 0.f;
+#pragma unroll 1
             for (int s = 0; s < S; ++s) {
                 const float ms = sw[s * Hq + hh];
                 const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
@@ -737,6 +762,7 @@ struct Mk {
         float2 acc[kP];
 #pragma unroll
         for (int v = 0; v < kP; ++v) acc[v] = make_float2(0.f, 0.f);
+#pragma unroll 1
         for (int s0 = 0; s0 < S && ok; s0 += kSG) {
             u64 a[kSG * kP], c[kSG * kP];
             unsigned pending = 0;
@@ -806,7 +832,9 @@ B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
         pf_live = true;
     }
     int cc = 0, pc = 0;
+#pragma unroll 1
     while (live) {
+#pragma unroll 1
         while (pc < cc + kStages + p.prefetch_chunks) {
             if (!pf_live) {
                 if (pf_wrapped) break;
@@ -830,6 +858,7 @@ B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
     }
     // Before leaving, wait (bounded) for the copies still in flight into this
     // CTA's shared memory: the last min(cc, kStages) issued chunks.
+#pragma unroll 1
     for (int c = max(0, cc - kStages); c < cc; ++c) mbar_wait_bounded(&sm.full[c % kStages], (c / kStages) & 1, nullptr);
 }
 
@@ -863,6 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
         static_assert(sizeof(MkLayer) % 8 == 0, "layer table copied in 8-byte words");
         const unsigned long long *src = reinterpret_cast<const unsigned long long *>(p.layers);
         unsigned long long *dst = reinterpret_cast<unsigned long long *>(s_layers);
+#pragma unroll 1
         for (int i = tid; i < p.n_layer * kWords; i += kThreads) dst[i] = src[i];
     }
     __syncthreads();
@@ -894,83 +924,69 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
     }
     const float *emb = p.tok_embd + static_cast<int64_t>(ok ? token : 0) * p.H;
     int64_t r0 = 0, r1 = 0;
-    for (int l = 0; l < p.n_layer && ok; ++l) {
-        const MkLayer &Lw = s_layers[l];
-        const int base = l * PH_PER_LAYER;
-        // QKV (layer 0 reads the token's embedding row)
-        stamp(p, base + PH_QKV, 3);
-        if (l == 0)
-            mk.load_act_plain(emb, p.H, Lw.attn_norm);
-        else if (!mk.load_act(p.tx, p.H, Lw.attn_norm, mk.tag(l - 1, PH_DOWN)))
-            break;
-        stamp(p, base + PH_QKV, 4);
-        PhaseW pw = phase_w(p, l, PH_QKV);
-        rows_of(pw.N, 1, b, G, r0, r1);
-        ok = mk.consume(pw, r0, r1, cc, base + PH_QKV);
-        for (int64_t r = r0 + tid; r < r1; r += kCT) st_tagged(p.tqkv + r, mk.row_sum(r - r0), mk.tag(l, PH_QKV));
-        stamp(p, base + PH_QKV, 5);
-        stamp(p, base + PH_QKV, 2);
-        if (!ok) break;
-        // attention
-        stamp(p, base + PH_ATTN, 3);
-        ok = mk.attention(l, n_past);
-        stamp(p, base + PH_ATTN, 5);
-        stamp(p, base + PH_ATTN, 2);
-        if (!ok) break;
-        // o_proj + residual (the residual rows are this CTA's own earlier writes)
-        stamp(p, base + PH_O, 3);
-        if (!mk.merge_attention(l, n_past)) break;
-        stamp(p, base + PH_O, 4);
-        pw = phase_w(p, l, PH_O);
-        rows_of(pw.N, 1, b, G, r0, r1);
-        ok = mk.consume(pw, r0, r1, cc, base + PH_O);
-        for (int64_t r = r0 + tid; r < r1; r += kCT) {
-            const float prev = l == 0 ? __ldg(emb + r) : tag_val(ld_tagged1(p.tx + r));
-            st_tagged(p.tx + r, mk.row_sum(r - r0) + prev, mk.tag(l, PH_O));
+    // One pass over the step's phases (per layer QKV, attention, o_proj, gate/up,
+    // down; then the LM head), each helper called from exactly one place so that
+    // the kernel's code stays small enough for the instruction cache.
+    const int n_ph = p.n_layer * PH_PER_LAYER + 1;
+    for (int q = 0; q < n_ph && ok; ++q) {
+        const int l = q / PH_PER_LAYER, ph = q % PH_PER_LAYER;
+        stamp(p, q, 3);
+        if (ph == PH_ATTN) {
+            ok = mk.attention(l, n_past);
+            stamp(p, q, 5);
+            stamp(p, q, 2);
+            continue;
         }
-        stamp(p, base + PH_O, 5);
-        stamp(p, base + PH_O, 2);
-        if (!ok) break;
-        // gate/up + SwiGLU
-        stamp(p, base + PH_GU, 3);
-        if (!mk.load_act(p.tx, p.H, Lw.ffn_norm, mk.tag(l, PH_O))) break;
-        stamp(p, base + PH_GU, 4);
-        pw = phase_w(p, l, PH_GU);
-        rows_of(pw.N, 2, b, G, r0, r1);
-        ok = mk.consume(pw, r0, r1, cc, base + PH_GU);
-        for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
-            const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
-            const float sg = gt / (1.0f + expf(-gt));
-            st_tagged(p.th + pr, up * sg, mk.tag(l, PH_GU));
+        const PhaseW pw = phase_w(p, l, ph);
+        rows_of(pw.N, pw.unit, b, G, r0, r1);
+        // phase input
+        if (ph == PH_O) {
+            ok = mk.merge_attention(l, n_past);
+        } else if (q == 0) {
+            mk.load_act_plain(emb, p.H, s_layers[0].attn_norm);
+        } else {
+            const bool lm = l == p.n_layer;
+            const u64 *src = ph == PH_DOWN ? p.th : p.tx;
+            const int64_t K = ph == PH_DOWN ? p.F : p.H;
+            const float *gamma = lm ? p.out_norm
+                                    : ph == PH_QKV ? s_layers[l].attn_norm : ph == PH_GU ? s_layers[l].ffn_norm : nullptr;
+            const uint32_t want = lm || ph == PH_QKV ? mk.tag(l - 1, PH_DOWN) : mk.tag(l, ph == PH_GU ? PH_O : PH_GU);
+            ok = mk.load_act(src, K, gamma, want);
         }
-        stamp(p, base + PH_GU, 5);
-        stamp(p, base + PH_GU, 2);
         if (!ok) break;
-        // down + residual
-        stamp(p, base + PH_DOWN, 3);
-        if (!mk.load_act(p.th, p.F, nullptr, mk.tag(l, PH_GU))) break;
-        stamp(p, base + PH_DOWN, 4);
-        pw = phase_w(p, l, PH_DOWN);
-        rows_of(pw.N, 1, b, G, r0, r1);
-        ok = mk.consume(pw, r0, r1, cc, base + PH_DOWN);
-        for (int64_t r = r0 + tid; r < r1; r += kCT)
-            st_tagged(p.tx + r, mk.row_sum(r - r0) + tag_val(ld_tagged1(p.tx + r)), mk.tag(l, PH_DOWN));
-        stamp(p, base + PH_DOWN, 5);
-        stamp(p, base + PH_DOWN, 2);
+        stamp(p, q, 4);
+        ok = mk.consume(pw, r0, r1, cc, q);
+        if (l == p.n_layer) break;  // LM head: the argmax below
+        // epilogue: tagged outputs of this CTA's rows
+        const uint32_t mine = mk.tag(l, ph);
+        if (ph == PH_GU) {
+#pragma unroll 1
+            for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
+                const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
+                const float sg = gt / (1.0f + expf(-gt));
+                st_tagged(p.th + pr, up * sg, mine);
+            }
+        } else {
+            u64 *dst = ph == PH_QKV ? p.tqkv : p.tx;
+#pragma unroll 1
+            for (int64_t r = r0 + tid; r < r1; r += kCT) {
+                float v = mk.row_sum(r - r0);
+                if (ph != PH_QKV)  // residual: this CTA's own earlier rows (layer 0: the embedding)
+                    v += (ph == PH_O && l == 0) ? __ldg(emb + r) : tag_val(ld_tagged1(p.tx + r));
+                st_tagged(dst + r, v, mine);
+            }
+        }
+        stamp(p, q, 5);
+        stamp(p, q, 2);
     }
     if (!ok || status_set(p.status)) return;
-
-    // ---- LM head + greedy argmax (first maximum; NaN / +inf -> -1)
     const int lm = p.n_layer * PH_PER_LAYER;
-    stamp(p, lm, 3);
-    if (!mk.load_act(p.tx, p.H, p.out_norm, mk.tag(p.n_layer - 1, PH_DOWN))) return;
-    stamp(p, lm, 4);
-    const PhaseW pw = phase_w(p, p.n_layer, 0);
-    rows_of(pw.N, 1, b, G, r0, r1);
-    if (!mk.consume(pw, r0, r1, cc, lm)) return;
+
+    // ---- LM head greedy argmax over the row sums (first maximum; NaN / +inf -> -1)
     float bv = -INFINITY;
     int64_t bi = INT64_MAX;
     bool bad = false;
+#pragma unroll 1
     for (int64_t r = r0 + tid; r < r1; r += kCT) {  // per thread: increasing rows
         const float v = mk.row_sum(r - r0);
         if (p.logits) p.logits[r] = v;
@@ -1004,6 +1020,7 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
         float v = s_bv[0];
         int64_t i = s_bi[0];
         bool anyb = s_bad[0];
+#pragma unroll 1
         for (int w = 1; w < kCW; ++w) {
             anyb |= s_bad[w] != 0;
             if (s_bv[w] > v || (s_bv[w] == v && s_bi[w] < i)) {
@@ -1024,6 +1041,7 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
         float v = -INFINITY;
         int32_t id = -1;
         bool anyb = false;
+#pragma unroll 1
         for (int c = 0; c < G; ++c) {  // CTAs own increasing row ranges
             const float cv = __ldcg(p.am_val + c);
             const int32_t ci = __ldcg(p.am_idx + c);
