@@ -49,7 +49,6 @@ constexpr int kMaxK = 3072;          // largest projection input (= one ring sta
 constexpr int kMaxLayers = 40;
 constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
 constexpr int kMaxSplits = 18;
-constexpr int64_t kDefaultPrefetchKB = 0;  // measured best on B200 (the ring alone keeps HBM busy)
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_PER_LAYER = 5 };
 
 struct PhaseW {
@@ -80,10 +79,12 @@ B200_HOST_DEVICE int rpc_for(int64_t K, int /*unit*/) {
     return static_cast<int>(r < kMaxRpc ? r : kMaxRpc);
 }
 
+// This CTA's row range of an N-row matrix, in whole units (32-bit arithmetic:
+// units * G stays below 2^31 for every supported shape).
 B200_DEVICE void rows_of(int64_t N, int unit, int b, int G, int64_t &r0, int64_t &r1) {
-    const int64_t units = N / unit;
-    r0 = units * b / G * unit;
-    r1 = units * (b + 1) / G * unit;
+    const unsigned units = static_cast<unsigned>(N / unit);
+    r0 = static_cast<int64_t>(units * static_cast<unsigned>(b) / static_cast<unsigned>(G)) * unit;
+    r1 = static_cast<int64_t>(units * static_cast<unsigned>(b + 1) / static_cast<unsigned>(G)) * unit;
 }
 
 // Walks this CTA's weight schedule chunk by chunk, in consumption order: per layer
@@ -817,35 +818,17 @@ template <int D>
 B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p);
 
 // The producer thread: streams the step's weight schedule through the ring (slot
-// c % kStages for chunk c, refilled as soon as its consumer warp releases it) and
-// keeps L2 bulk prefetches prefetch_chunks ahead of the copies; past the LM head
-// the prefetches warm the head of the schedule for the next step (same weights).
-// It never waits on activations, so HBM keeps streaming while the consumers wait
-// for other CTAs' outputs. Every wait is bounded and abandoned on error.
+// c % kStages for chunk c, refilled as soon as its consumer warp releases it). It
+// never waits on activations, so HBM keeps streaming while the consumers wait for
+// other CTAs' outputs; 16 slots of 12 KB per SM keep enough bytes in flight.
+// Every wait is bounded and abandoned on error.
 B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
     const uint64_t pol = policy_evict_first();
-    Cursor cp, pf;
+    Cursor cp;
     bool live = cp.start(p, b, G, 0);
-    bool pf_live = false, pf_wrapped = false;
-    if (live) {
-        pf = cp;
-        pf_live = true;
-    }
-    int cc = 0, pc = 0;
+    int cc = 0;
 #pragma unroll 1
     while (live) {
-#pragma unroll 1
-        while (pc < cc + kStages + p.prefetch_chunks) {
-            if (!pf_live) {
-                if (pf_wrapped) break;
-                pf_live = pf.start(p, b, G, 0);
-                pf_wrapped = true;
-                if (!pf_live) break;
-            }
-            if (pc >= cc + kStages) prefetch_l2_bulk(pf.src(), pf.bytes());  // the ring covers the rest
-            ++pc;
-            pf_live = pf.advance(p, b, G, 1);
-        }
         const int s = cc % kStages;
         // (a consumer that stopped leaves its slot unreleased: the wait sees the
         // status word then; no per-chunk global load on the issue path)
@@ -1077,17 +1060,6 @@ size_t smem_bytes(int D) {
 
 int mk_grid() { return device_sm_count(); }
 
-// L2 prefetch distance per CTA beyond the ring, in ring chunks
-// (B200_MK_PREFETCH_KB overrides the default distance in KB).
-int mk_prefetch_chunks() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = std::getenv("B200_MK_PREFETCH_KB");
-        const long long kb = (e && *e) ? std::max(0LL, std::atoll(e)) : kDefaultPrefetchKB;
-        v = static_cast<int>(kb * 1024 / (kStageFloats * 4));
-    }
-    return v;
-}
 int mk_max_splits() { return kMaxSplits; }
 size_t mk_po_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * p.D; }
 size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * 2; }
@@ -1098,6 +1070,10 @@ bool mk_supported(const MkParams &p) {
     if (p.Hkv <= 0 || p.Hq % p.Hkv || kCW % (p.Hq / p.Hkv)) return false;
     const int G = mk_grid();
     if (p.Hkv > G) return false;
+    // 32-bit row-range arithmetic (rows_of)
+    const int64_t nmax = std::max<int64_t>({static_cast<int64_t>(p.V), 2 * static_cast<int64_t>(p.F),
+                                            static_cast<int64_t>(p.Hq + 2 * p.Hkv) * p.D});
+    if (nmax * (G + 1) >= (1LL << 32)) return false;
     // merge: scratch in sm.part, (split, head) pairs and output pairs per thread
     if (2 * kMaxSplits * p.Hq + p.Hq > kPartFloats || kMaxSplits * p.Hq > 2 * kCT || p.Hq * p.D > 8 * kCT)
         return false;
@@ -1124,7 +1100,6 @@ cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     MkParams args = p;
-    args.prefetch_chunks = mk_prefetch_chunks();
     void *kargs[] = {&args};
     return cudaLaunchCooperativeKernel(kern, dim3(mk_grid()), dim3(kThreads), kargs, smem, stream);
 }

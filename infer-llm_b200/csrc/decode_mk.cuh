@@ -36,8 +36,6 @@ struct MkParams {
     int32_t *am_idx = nullptr;
     unsigned *am_counter = nullptr;    // zero at launch; the last CTA re-zeroes it
     unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
-    int prefetch_chunks = 0;           // per CTA: L2 prefetch distance beyond the ring, in ring
-                                       // chunks (set by mk_launch)
 };
 
 // True if the megakernel supports this model shape on this device.
@@ -49,7 +47,5 @@ size_t mk_pml_words(const MkParams &p);
 // Enqueues the cooperative launch.
 cudaError_t mk_launch(const MkParams &p, cudaStream_t stream);
 int mk_grid();
-// L2 prefetch distance of each CTA ahead of its ring copies, in ring chunks.
-int mk_prefetch_chunks();
 
 }  // namespace b200
