@@ -237,7 +237,7 @@ B200_DEVICE bool poll_pairs(unsigned pending, const int32_t *status_p, int32_t *
                 return false;
             }
         }
-        __nanosleep(64);
+        // polls back to back: each retry already waits one L2 round trip
 #pragma unroll
         for (int j = 0; j < N; ++j)
             if ((still >> j) & 1u) reload(j);
