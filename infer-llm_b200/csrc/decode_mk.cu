@@ -49,6 +49,7 @@ constexpr int kMaxK = 3072;          // largest projection input (= one ring sta
 constexpr int kMaxLayers = 40;
 constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
 constexpr int kMaxSplits = 18;
+constexpr int kMaxGq = 4;            // query heads per KV head (attention registers)
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_PER_LAYER = 5 };
 
 struct PhaseW {
@@ -252,8 +253,7 @@ struct Smem {
     float *ring;   // [kStages][kStageFloats]
     float *xs;     // [kMaxK] phase input activation
     float *part;   // [kPartFloats]
-    float *qs;     // [kCW][D] per-warp rotated query
-    float *wpart;  // [kCW][D + 2] per-warp attention partial (o, m, l)
+    float *qs;     // [Gq][D] rotated queries of the KV group (attention)
 };
 
 template <int D>
@@ -545,13 +545,17 @@ struct Mk {
         return __all_sync(0xffffffffu, ok);
     }
 
-    // ---- attention for one (KV head, split): fused q/k norm + RoPE, KV append,
-    // online softmax over the split's keys in batches of kTB. The first batch of
-    // cached keys/values is in flight while the queries and the new token are
-    // normalised; the new token's k/v come from shared memory (the cache row is
-    // written for later steps only). Partials go out as tagged words.
+    // ---- attention for one (KV head g, split s): the split's keys are cut into
+    // kCW sub-ranges, one per warp, and every warp scores its keys against all Gq
+    // query heads of the group (each cached K/V row is read once per CTA). Warps
+    // 0..Gq-1 normalise + rotate the queries, warp Gq the new token's key and warp
+    // Gq+1 copies its value (last split only; both are appended to the cache for
+    // later steps and used from shared memory here). The first batch of cached
+    // K/V rows is in flight while that happens. Online softmax in batches of kTB
+    // keys; the kCW sub-range partials are merged in order and the split partial
+    // (o, max, sum) per query head goes out as tagged words.
     B200_DEVICE bool attention(int layer, int64_t n_past) {
-        constexpr int kTB = 8;
+        constexpr int kTB = 4;
         const MkLayer &Lw = s_layers[layer];
         const uint32_t want = tag(layer, PH_QKV), mine = tag(layer, PH_ATTN);
         const int Gq = p.Hq / p.Hkv;
@@ -560,16 +564,15 @@ struct Mk {
         if (b >= p.Hkv * S) return true;
         __shared__ int s_bad;
         if (tid == 0) s_bad = 0;
-        named_sync(1, kCT);  // sm.part (new k/v) is free: the QKV epilogue has read it
+        named_sync(1, kCT);  // shared scratch is free: the QKV epilogue has read sm.part
         const int g = b / S, s = b % S;
         const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
         const bool last = (s == S - 1);
         const int64_t tok = static_cast<int64_t>(p.Hkv) * D;  // cache token stride
-        const int qh = warp % Gq, sub = warp / Gq, nsub = kCW / Gq;
-        const int h = g * Gq + qh;
-        const int64_t t0 = j0 + (j1 - j0) * sub / nsub, t1 = j0 + (j1 - j0) * (sub + 1) / nsub;
+        const int64_t t0 = j0 + (j1 - j0) * warp / kCW, t1 = j0 + (j1 - j0) * (warp + 1) / kCW;
         const float *kb = Lw.kc + g * D + lane * E, *vb = Lw.vc + g * D + lane * E;
-        float *kn = sm.part, *vn = sm.part + D;  // the new token's k, v
+        float *kn = sm.part + kPartFloats - 2 * D, *vn = kn + D;  // the new token's k, v
+        float *wpart = sm.xs;  // [kCW][Gq][D + 2] sub-range partials (xs and part are contiguous)
         float kv[kTB][E], vv[kTB][E];
         auto load_batch = [&](int64_t t, int n) {
 #pragma unroll
@@ -585,21 +588,18 @@ struct Mk {
         };
         load_batch(t0, static_cast<int>(min64(kTB, t1 - t0)));
         bool ok = true;
-        // queries (every warp, its head) and, in warp 0 of the last split, the new
-        // token's key: one call site for the norm + RoPE code
-#pragma unroll 1
-        for (int pass = (last && warp == 0) ? 0 : 1; pass < 2; ++pass) {
-            const bool key = pass == 0;
-            ok = norm_rope_head(p.tqkv + (key ? p.Hq + g : h) * D, want, key ? Lw.k_norm : Lw.q_norm, n_past,
-                                key ? kn : sm.qs + warp * D) && ok;
-            if (key) {
+        const bool isq = warp < Gq, isk = last && warp == Gq;
+        if (isq || isk) {  // one call site for the norm + RoPE code
+            ok = norm_rope_head(p.tqkv + (isq ? g * Gq + warp : p.Hq + g) * D, want, isq ? Lw.q_norm : Lw.k_norm,
+                                n_past, isq ? sm.qs + warp * D : kn);
+            if (isk) {
                 __syncwarp();
                 float *dst = Lw.kc + n_past * tok + g * D;
 #pragma unroll 1
                 for (int d = lane; d < D; d += 32) st_keep(dst + d, kn[d], keep);
             }
         }
-        if (last && warp == 1) {  // new token v as is
+        if (last && warp == Gq + 1) {  // new token v as is
             float v[E];
             ok = __all_sync(0xffffffffu, read_head_lane(p.tqkv + (p.Hq + p.Hkv + g) * D, want, v));
             float *vdst = Lw.vc + n_past * tok + g * D;
@@ -612,13 +612,18 @@ struct Mk {
         if (!ok && lane == 0) s_bad = 1;
         named_sync(1, kCT);
         if (s_bad) return false;
-        float q[E];
+        float q[kMaxGq][E], m[kMaxGq], l[kMaxGq], o[kMaxGq][E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) q[e] = sm.qs[warp * D + lane * E + e];
+        for (int hh = 0; hh < kMaxGq; ++hh) {
+            m[hh] = -INFINITY;
+            l[hh] = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                q[hh][e] = hh < Gq ? sm.qs[hh * D + lane * E + e] : 0.f;
+                o[hh][e] = 0.f;
+            }
+        }
         const float scale = 1.0f / sqrtf(static_cast<float>(D));
-        float m = -INFINITY, l = 0.f, o[E];
-#pragma unroll
-        for (int e = 0; e < E; ++e) o[e] = 0.f;
 #pragma unroll 1
         for (int64_t t = t0; t < t1; t += kTB) {
             const int n = static_cast<int>(min64(kTB, t1 - t));
@@ -635,58 +640,71 @@ struct Mk {
                         }
                     }
             }
-            float sc[kTB];
+            float sc[kTB][kMaxGq];
 #pragma unroll
-            for (int j = 0; j < kTB; ++j) {
-                float d = 0.f;
+            for (int j = 0; j < kTB; ++j)
 #pragma unroll
-                for (int e = 0; e < E; ++e) d = fmaf(q[e], kv[j][e], d);
-                sc[j] = d;
-            }
+                for (int hh = 0; hh < kMaxGq; ++hh) {
+                    float d = 0.f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) d = fmaf(q[hh][e], kv[j][e], d);
+                    sc[j][hh] = d;
+                }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-                for (int j = 0; j < kTB; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], off);
-            float bm = m;
+                for (int j = 0; j < kTB; ++j)
 #pragma unroll
-            for (int j = 0; j < kTB; ++j) {
-                sc[j] = j < n ? sc[j] * scale : -INFINITY;
-                bm = fmaxf(bm, sc[j]);
-            }
-            const float corr = (m == -INFINITY) ? 0.f : expf(m - bm);
-            l *= corr;
+                    for (int hh = 0; hh < kMaxGq; ++hh)
+                        if (hh < Gq) sc[j][hh] += __shfl_xor_sync(0xffffffffu, sc[j][hh], off);
 #pragma unroll
-            for (int e = 0; e < E; ++e) o[e] *= corr;
+            for (int hh = 0; hh < kMaxGq; ++hh) {
+                if (hh >= Gq) continue;
+                float bm = m[hh];
 #pragma unroll
-            for (int j = 0; j < kTB; ++j) {
-                if (j < n) {
-                    const float pr = expf(sc[j] - bm);
-                    l += pr;
-#pragma unroll
-                    for (int e = 0; e < E; ++e) o[e] = fmaf(pr, vv[j][e], o[e]);
+                for (int j = 0; j < kTB; ++j) {
+                    sc[j][hh] = j < n ? sc[j][hh] * scale : -INFINITY;
+                    bm = fmaxf(bm, sc[j][hh]);
                 }
-            }
-            m = bm;
-        }
-        float *wp = sm.wpart + warp * (D + 2);
+                const float corr = (m[hh] == -INFINITY) ? 0.f : expf(m[hh] - bm);
+                l[hh] *= corr;
 #pragma unroll
-        for (int e = 0; e < E; ++e) wp[lane * E + e] = o[e];
-        if (lane == 0) {
-            wp[D] = m;
-            wp[D + 1] = l;
+                for (int e = 0; e < E; ++e) o[hh][e] *= corr;
+#pragma unroll
+                for (int j = 0; j < kTB; ++j) {
+                    if (j < n) {
+                        const float pr = expf(sc[j][hh] - bm);
+                        l[hh] += pr;
+#pragma unroll
+                        for (int e = 0; e < E; ++e) o[hh][e] = fmaf(pr, vv[j][e], o[hh][e]);
+                    }
+                }
+                m[hh] = bm;
+            }
+        }
+#pragma unroll
+        for (int hh = 0; hh < kMaxGq; ++hh) {
+            if (hh >= Gq) continue;
+            float *wp = wpart + (warp * Gq + hh) * (D + 2);
+#pragma unroll
+            for (int e = 0; e < E; ++e) wp[lane * E + e] = o[hh][e];
+            if (lane == 0) {
+                wp[D] = m[hh];
+                wp[D + 1] = l[hh];
+            }
         }
         named_sync(1, kCT);
-        // combine the token sub-ranges of each head in order -> the split's partial
+        // merge the kCW sub-ranges of each head in order -> the split's partial
 #pragma unroll 1
         for (int i = tid; i < Gq * D; i += kCT) {
             const int hh = i / D, d = i % D;
             float M = -INFINITY;
 #pragma unroll 1
-            for (int u = 0; u < nsub; ++u) M = fmaxf(M, sm.wpart[(u * Gq + hh) * (D + 2) + D]);
+            for (int u = 0; u < kCW; ++u) M = fmaxf(M, wpart[(u * Gq + hh) * (D + 2) + D]);
             float lsum = 0.f, os = 0.f;
 #pragma unroll 1
-            for (int u = 0; u < nsub; ++u) {
-                const float *w = sm.wpart + (u * Gq + hh) * (D + 2);
+            for (int u = 0; u < kCW; ++u) {
+                const float *w = wpart + (u * Gq + hh) * (D + 2);
                 if (w[D] == -INFINITY) continue;
                 const float f = expf(w[D] - M);
                 lsum = fmaf(f, w[D + 1], lsum);
@@ -699,6 +717,7 @@ struct Mk {
                 st_tagged(p.tpml + sh * 2 + 1, lsum, mine);
             }
         }
+        named_sync(1, kCT);  // sm.xs (the partials) is read before the o_proj input overwrites it
         return true;
     }
 
@@ -856,7 +875,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
     sm.xs = sm.ring + kStages * kStageFloats;
     sm.part = sm.xs + kMaxK;
     sm.qs = sm.part + kPartFloats;
-    sm.wpart = sm.qs + kCW * D;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x, G = gridDim.x;
@@ -1052,8 +1070,7 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
 
 size_t smem_bytes(int D) {
     return 256 + static_cast<size_t>(kStages) * kStageFloats * 4 + static_cast<size_t>(kMaxK) * 4 +
-           static_cast<size_t>(kPartFloats) * 4 + static_cast<size_t>(kCW) * D * 4 +
-           static_cast<size_t>(kCW) * (D + 2) * 4;
+           static_cast<size_t>(kPartFloats) * 4 + static_cast<size_t>(kMaxGq) * D * 4;
 }
 
 }  // namespace
@@ -1067,7 +1084,9 @@ size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) 
 bool mk_supported(const MkParams &p) {
     if (p.D != 64 && p.D != 128) return false;
     if (p.n_layer < 1 || p.n_layer > kMaxLayers) return false;
-    if (p.Hkv <= 0 || p.Hq % p.Hkv || kCW % (p.Hq / p.Hkv)) return false;
+    if (p.Hkv <= 0 || p.Hq % p.Hkv || p.Hq / p.Hkv > kMaxGq) return false;
+    // attention scratch: kCW x Gq sub-range partials in xs + part below the new k/v
+    if (kCW * (p.Hq / p.Hkv) * (p.D + 2) > kMaxK + kPartFloats - 2 * p.D) return false;
     const int G = mk_grid();
     if (p.Hkv > G) return false;
     // 32-bit row-range arithmetic (rows_of)
