@@ -101,6 +101,18 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def max_over_ranks(value: float, world: int) -> float:
+    """The slowest rank's time: every timing the bench reports is the max over ranks."""
+    if world <= 1:
+        return float(value)
+    import torch
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([float(value)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -246,12 +258,7 @@ def run_b200(args):
         toks = eng.generate(steps)
         ev1.record(stream)
         barrier()
-    ms = ev0.elapsed_time(ev1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), world)
     units = steps * (1 if tp else world)  # TP: one stream of tokens; replicas: one per rank
     value = units / (ms_max / 1e3)
     # ---- e2e through the public call with host buffers (H2D id, D2H token per step)
@@ -266,11 +273,7 @@ def run_b200(args):
         host_tok[0] = tok
     e1.record(stream)
     barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
     e2e = units / (e2e_ms / 1e3)
     # ---- per-op breakdown of one eager decode step (events after each launch)
     ops = {}

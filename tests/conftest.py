@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-for p in (os.path.join(REPO, "oracle"), os.path.join(REPO, "infer-llm_b200"), os.path.join(REPO, "tests", "golden")):
+for p in (REPO, os.path.join(REPO, "oracle"), os.path.join(REPO, "infer-llm_b200"), os.path.join(REPO, "tests", "golden")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
