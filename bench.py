@@ -305,7 +305,8 @@ def run_b200(args):
                                f"{PROMPT_LEN}, positions {PROMPT_LEN}..{PROMPT_LEN + steps - 1}",
                    "weights": f"seeded N(0,0.02) ({'GGUF' if args.model == '0.6b' else 'on-device Philox'}, seed {SEED})",
                    "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
-                   "l2": "inputs larger than L2 (2.38 GB of weights streamed per step)"},
+                   "l2": f"inputs larger than L2 ({cfg.weight_bytes_per_token / 1e9:.2f} GB of weights "
+                         f"streamed per step{' over all ranks' if tp else ''})"},
         "ttft_ms": round(float(np.median(ttft)), 3),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": steps * launches,
@@ -328,7 +329,8 @@ def run_b200(args):
         res["multi_kernel_gemv_roofline_eager"] = {
             "kernel": "gemv kernels of one eager multi-kernel step", "achieved": round(achieved, 1),
             "unit": "GB/s", "frac": round(achieved / hbm, 4)}
-    res["step_roofline"] = {"achieved": round(step_gbs, 1), "frac": round(step_gbs / hbm, 4),
+    # tensor parallel: the step's bytes are spread over `world` GPUs' HBM
+    res["step_roofline"] = {"achieved": round(step_gbs, 1), "frac": round(step_gbs / (hbm * (world if tp else 1)), 4),
                             "bytes_per_step": step_b}
     if launches != 1 and ops:
         res["roofline"] = dict(res["multi_kernel_gemv_roofline_eager"], bound="hbm", peak=hbm,
