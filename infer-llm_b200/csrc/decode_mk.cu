@@ -49,6 +49,7 @@ constexpr int kMaxK = 3072;          // largest projection input (= one ring sta
 constexpr int kMaxLayers = 40;
 constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
 constexpr int kMaxSplits = 18;
+constexpr int kDefaultInflight = 8;  // measured: 8 copies (96 KB) per SM keep HBM busy; 3 starve the LM head
 constexpr int kMaxGq = 4;            // query heads per KV head (attention registers)
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_PER_LAYER = 5 };
 
@@ -845,9 +846,21 @@ B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
     const uint64_t pol = policy_evict_first();
     Cursor cp;
     bool live = cp.start(p, b, G, 0);
-    int cc = 0;
+    int cc = 0, landed = 0;  // chunks issued / chunks known to have landed
 #pragma unroll 1
     while (live) {
+        // At most max_inflight copies outstanding: enough bytes in flight for this
+        // SM's share of HBM bandwidth, and no deeper queue in front of the
+        // consumers' own latency-critical loads (activations, KV rows).
+#pragma unroll 1
+        while (cc - landed >= p.max_inflight) {
+            if (!mbar_wait_bounded(&sm.full[landed % kStages], (landed / kStages) & 1, p.status)) {
+                live = false;
+                break;
+            }
+            ++landed;
+        }
+        if (!live) break;
         const int s = cc % kStages;
         // (a consumer that stopped leaves its slot unreleased: the wait sees the
         // status word then; no per-chunk global load on the issue path)
@@ -1077,6 +1090,17 @@ size_t smem_bytes(int D) {
 
 int mk_grid() { return device_sm_count(); }
 
+// Ring copies in flight per CTA (B200_MK_INFLIGHT overrides the default).
+int mk_max_inflight() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = std::getenv("B200_MK_INFLIGHT");
+        const int x = (e && *e) ? std::atoi(e) : kDefaultInflight;
+        v = std::min(std::max(x, 1), kStages);
+    }
+    return v;
+}
+
 int mk_max_splits() { return kMaxSplits; }
 size_t mk_po_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * p.D; }
 size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * 2; }
@@ -1119,6 +1143,7 @@ cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     MkParams args = p;
+    args.max_inflight = mk_max_inflight();
     void *kargs[] = {&args};
     return cudaLaunchCooperativeKernel(kern, dim3(mk_grid()), dim3(kThreads), kargs, smem, stream);
 }

@@ -36,6 +36,7 @@ struct MkParams {
     int32_t *am_idx = nullptr;
     unsigned *am_counter = nullptr;    // zero at launch; the last CTA re-zeroes it
     unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
+    int max_inflight = 16;             // ring copies outstanding per CTA (set by mk_launch)
 };
 
 // True if the megakernel supports this model shape on this device.
@@ -47,5 +48,6 @@ size_t mk_pml_words(const MkParams &p);
 // Enqueues the cooperative launch.
 cudaError_t mk_launch(const MkParams &p, cudaStream_t stream);
 int mk_grid();
+int mk_max_inflight();
 
 }  // namespace b200
