@@ -114,6 +114,8 @@ struct b200_engine {
     float *am_val = nullptr;
     int32_t *am_idx = nullptr;
     unsigned *am_counter = nullptr;
+    float *gemm_ws = nullptr;  // split-K partials of the prefill GEMMs
+    int64_t gemm_ws_floats = 0;
     int am_slots = 0;  // per-CTA argmax partials of the LM head GEMV (+1 local winner slot)
     float *tp_pairs = nullptr;  // [world][2] (value, index) for the vocab-sharded argmax
     // state
@@ -387,6 +389,8 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         g.N = e->qkv_rows;
         g.K = H;
         g.epi = GEMM_STORE;
+        g.ws = e->gemm_ws;
+        g.ws_floats = e->gemm_ws_floats;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(g, st, pdl) : gemm_ffma_launch(g, st, pdl));
 
         QkNormRopeArgs r;
@@ -443,6 +447,8 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         o.N = H;
         o.K = static_cast<int64_t>(e->Hq) * D;
         o.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
+        o.ws = e->gemm_ws;
+        o.ws_floats = e->gemm_ws_floats;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(o, st, pdl) : gemm_ffma_launch(o, st, pdl));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
 
@@ -457,6 +463,8 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         gu.N = 2 * static_cast<int64_t>(e->F);
         gu.K = H;
         gu.epi = GEMM_SWIGLU;
+        gu.ws = e->gemm_ws;
+        gu.ws_floats = e->gemm_ws_floats;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(gu, st, pdl) : gemm_ffma_launch(gu, st, pdl));
 
         GemmArgs dn;
@@ -470,6 +478,8 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         dn.N = H;
         dn.K = e->F;
         dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
+        dn.ws = e->gemm_ws;
+        dn.ws_floats = e->gemm_ws_floats;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(dn, st, pdl) : gemm_ffma_launch(dn, st, pdl));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
     }
@@ -626,6 +636,9 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t o_pairs = take(2 * W + 64);
     e->trace_cap = 5 * c.n_layer + 8;
     const size_t o_trace = take(2 * 8 * static_cast<int64_t>(e->trace_cap));
+    // split-K workspace of the prefill GEMMs: 8 Mi floats (bounded by the launcher)
+    e->gemm_ws_floats = int64_t(8) << 20;
+    const size_t o_gws = take(e->gemm_ws_floats);
     const size_t o_mkl = take(static_cast<int64_t>(sizeof(MkLayer) / 4 + 1) * NL);
     MkParams shape;
     shape.Hq = e->Hq;
@@ -688,6 +701,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->am_counter = reinterpret_cast<unsigned *>(e->act_arena + o_amc);
     e->tp_pairs = af(o_pairs);
     e->trace_buf = reinterpret_cast<unsigned long long *>(e->act_arena + o_trace);
+    e->gemm_ws = af(o_gws);
     e->mk_layers = reinterpret_cast<MkLayer *>(e->act_arena + o_mkl);
     auto aw = [&](size_t o) { return reinterpret_cast<unsigned long long *>(e->act_arena + o); };
     e->mk.tx = aw(o_tx);

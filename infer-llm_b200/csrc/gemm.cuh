@@ -20,6 +20,12 @@ struct GemmArgs {
     const float *r = nullptr;  // residual [M][ldc]
     int64_t M = 0, N = 0, K = 0;
     int epi = GEMM_STORE;
+    // Optional split-K workspace (floats). When the M x N tile grid is too small to
+    // fill the GPU, the FFMA GEMM splits K, writes per-split partials here and
+    // reduces them in split order (deterministic) with the epilogue.
+    float *ws = nullptr;
+    int64_t ws_floats = 0;
+    int64_t k_split = 0;  // set by the launcher: K per split (0 = no split)
 };
 
 // Exact F32 FFMA tiled GEMM (any M; K % 4 == 0).

@@ -5,7 +5,10 @@
 // Global tiles are read with 128-bit loads into registers one K-step ahead and
 // stored transposed into a double-buffered shared tile. Epilogues fuse the
 // residual add and SwiGLU of the reference graph (Qwen3.cpp:97,109-118).
+#include <algorithm>
+
 #include "gemm.cuh"
+#include "gemv.cuh"
 
 namespace b200 {
 namespace {
@@ -26,7 +29,10 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
     const int tx = tid & 15, ty = tid >> 4;
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
     const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
-    const int64_t K = a.K;
+    const int64_t K = a.K;  // row stride of W and X's K extent
+    // split-K: this CTA's K range [kbeg, kend)
+    const int64_t kbeg = a.k_split ? static_cast<int64_t>(blockIdx.z) * a.k_split : 0;
+    const int64_t kend = a.k_split ? min64(K, kbeg + a.k_split) : K;
 
     // X tile: BM rows x 4 float4; W tile: 128 rows x 4 float4 (2 per thread)
     float4 ra[A_LD > 0 ? A_LD : 1], rb[2];
@@ -37,13 +43,13 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
                 const int f = tid + i * NT;
                 const int row = f >> 2, k4 = f & 3;
                 const int64_t gm = m0 + row, gk = k0 + k4 * 4;
-                ra[i] = (gm < a.M && gk < K) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
+                ra[i] = (gm < a.M && gk < kend) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         } else if (tid < BM * 4) {
             const int row = tid >> 2, k4 = tid & 3;
             const int64_t gm = m0 + row, gk = k0 + k4 * 4;
-            ra[0] = (gm < a.M && gk < K) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
+            ra[0] = (gm < a.M && gk < kend) ? *reinterpret_cast<const float4 *>(a.x + gm * a.ldx + gk)
                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
@@ -51,7 +57,7 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
             const int f = tid + i * NT;
             const int row = f >> 2, k4 = f & 3;
             const int64_t gn = n0 + row, gk = k0 + k4 * 4;
-            rb[i] = (gn < a.N && gk < K) ? ld_stream4(reinterpret_cast<const float4 *>(a.w + gn * K + gk))
+            rb[i] = (gn < a.N && gk < kend) ? ld_stream4(reinterpret_cast<const float4 *>(a.w + gn * K + gk))
                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     };
@@ -96,13 +102,13 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
         return ty * TM + i;
     };
 
-    const int64_t nk = (K + BK - 1) / BK;
-    load_tiles(0);
+    const int64_t nk = (kend - kbeg + BK - 1) / BK;
+    load_tiles(kbeg);
     store_tiles(0);
     __syncthreads();
     for (int64_t kt = 0; kt < nk; ++kt) {
         const int buf = kt & 1;
-        if (kt + 1 < nk) load_tiles((kt + 1) * BK);
+        if (kt + 1 < nk) load_tiles(kbeg + (kt + 1) * BK);
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
             float av[TM], bv[8];
@@ -134,6 +140,22 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
     }
 
     // epilogue
+    if (a.k_split) {  // raw partial sums of this split: ws[z][M][N]
+        float *ws = a.ws + static_cast<int64_t>(blockIdx.z) * a.M * a.N;
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int64_t gm = m0 + row_of(i);
+            if (gm >= a.M) continue;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t col = n0 + h * 64 + tx * 4 + j;
+                    if (col < a.N) ws[gm * a.N + col] = acc[i][h * 4 + j];
+                }
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const int64_t gm = m0 + row_of(i);
@@ -166,9 +188,63 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
     }
 }
 
+// Sums the split partials in split order and applies the epilogue (same
+// arithmetic as sgemm_kernel's): one thread per output (per gate/up pair for SwiGLU).
+template <int EPI>
+__global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
+    grid_launch_dependents();
+    grid_wait();
+    const int64_t per_row = EPI == GEMM_SWIGLU ? a.N / 2 : a.N;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= a.M * per_row) return;
+    const int64_t m = i / per_row, n = i % per_row;
+    const int64_t plane = a.M * a.N;
+    if (EPI == GEMM_SWIGLU) {
+        float g = 0.f, u = 0.f;
+        for (int z = 0; z < splits; ++z) {
+            g += a.ws[z * plane + m * a.N + 2 * n];
+            u += a.ws[z * plane + m * a.N + 2 * n + 1];
+        }
+        const float sg = g / (1.0f + expf(-g));
+        a.c[m * a.ldc + n] = u * sg;
+    } else {
+        float v = 0.f;
+        for (int z = 0; z < splits; ++z) v += a.ws[z * plane + m * a.N + n];
+        if (EPI == GEMM_RESIDUAL) v = v + a.r[m * a.ldc + n];
+        a.c[m * a.ldc + n] = v;
+    }
+}
+
 template <int BM>
-cudaError_t launch_bm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+cudaError_t launch_bm(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
+    GemmArgs a = a_in;
     dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + BM - 1) / BM));
+    // Split K when the tile grid leaves most SMs idle (decode-sized prompts): aim
+    // for about two CTAs per SM, at least 256 of K per split, partials in a.ws.
+    a.k_split = 0;
+    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y, target = 2 * device_sm_count();
+    if (a.ws && tiles < target && a.K >= 512) {
+        int64_t splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
+        while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
+        if (splits > 1) {
+            a.k_split = ((a.K + splits - 1) / splits + BK - 1) / BK * BK;
+            grid.z = static_cast<unsigned>((a.K + a.k_split - 1) / a.k_split);
+        }
+    }
+    if (a.k_split) {
+        cudaError_t e = b200_launch(sgemm_kernel<BM, GEMM_STORE>, grid, dim3(NT), 0, stream, pdl, a);
+        if (e != cudaSuccess) return e;
+        const int splits = static_cast<int>(grid.z);
+        const int64_t outs = a.M * (a.epi == GEMM_SWIGLU ? a.N / 2 : a.N);
+        const dim3 rg(static_cast<unsigned>((outs + 255) / 256));
+        switch (a.epi) {
+            case GEMM_STORE: return b200_launch(splitk_reduce_kernel<GEMM_STORE>, rg, dim3(256), 0, stream, pdl, a, splits);
+            case GEMM_RESIDUAL:
+                return b200_launch(splitk_reduce_kernel<GEMM_RESIDUAL>, rg, dim3(256), 0, stream, pdl, a, splits);
+            case GEMM_SWIGLU: return b200_launch(splitk_reduce_kernel<GEMM_SWIGLU>, rg, dim3(256), 0, stream, pdl, a, splits);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (a.epi) {
         case GEMM_STORE: return b200_launch(sgemm_kernel<BM, GEMM_STORE>, grid, dim3(NT), 0, stream, pdl, a);
         case GEMM_RESIDUAL: return b200_launch(sgemm_kernel<BM, GEMM_RESIDUAL>, grid, dim3(NT), 0, stream, pdl, a);
