@@ -310,7 +310,7 @@ def run_b200(args):
                          f"streamed per step{' over all ranks' if tp else ''})"},
         "ttft_ms": round(float(np.median(ttft)), 3),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        "gpu_launches": steps * launches,
+        "gpu_launches": steps * launches * world,  # every rank launches its own
         "clocks": clk.summary(),
     }
     step_b = step_bytes(cfg, ctx_mid)
