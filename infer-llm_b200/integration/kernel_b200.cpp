@@ -1,0 +1,109 @@
+// Drop-in replacement for the reference's src/kernels/cuda/kernel_f32.cu.
+//
+// A maintainer of the reference keeps its CUDA backend (src/backends/cuda_backend.cpp,
+// which dispatches every graph node to CUDA_F32::compute_<op>, cuda_backend.cpp:211-238)
+// and swaps kernel_f32.cu for this file: each compute_<op>(Tensor *dst, cudaStream_t)
+// of include/kernels/cuda/kernel_f32.hpp:8-28 becomes one call into the B200 C ABI
+// (include/b200_infer.h) with the tensor's raw pointers, sizes and strides. Built
+// against the reference headers with INFERLLM_WITH_CUDA defined and linked with
+// libb200infer.so (oracle/Makefile target `ref-b200` does exactly that for the
+// end-to-end drop-in test).
+//
+// Semantics follow the reference kernels: mul_mat out[N, M] = W[K, N]^T x[K, M]
+// (kernel_f32.cu:180-205); RMSNorm over dims[0] with eps in op_params[0] (60-90);
+// RoPE with the GraphContext angle table as src[2] (273-301); attention with
+// AttnParams in op_params, scale defaulting to 1/sqrt(head_dim) (452-511); CPY /
+// RESHAPE are device copies, VIEW is a no-op (210-240, 305-326).
+#include <cmath>
+#include <cstring>
+
+#include "b200_infer.h"
+#include "kernels/cuda/kernel_f32.hpp"
+#include "op_params.hpp"
+#include "tensor.hpp"
+
+namespace {
+
+cudaError_t as_cuda(int rc) {
+    switch (rc) {
+        case B200_OK: return cudaSuccess;
+        case B200_ERR_INVALID_ARGUMENT:
+        case B200_ERR_OUT_OF_RANGE: return cudaErrorInvalidValue;
+        case B200_ERR_NOT_SUPPORTED: return cudaErrorNotSupported;
+        case B200_ERR_NO_MEMORY: return cudaErrorMemoryAllocation;
+        default: return cudaErrorUnknown;
+    }
+}
+
+const float *cf(const Tensor *t) { return static_cast<const float *>(t->data); }
+float *mf(Tensor *t) { return static_cast<float *>(t->data); }
+
+}  // namespace
+
+namespace CUDA_F32 {
+
+cudaError_t compute_mul_mat(Tensor *dst, cudaStream_t s) {
+    const Tensor *w = dst->src[0], *x = dst->src[1];
+    if (w->dims[0] != x->dims[0] || w->dims[1] != dst->dims[0] || x->dims[1] != dst->dims[1])
+        return cudaErrorInvalidValue;
+    return as_cuda(b200_mul_mat(cf(w), cf(x), mf(dst), w->dims[0], w->dims[1], x->dims[1], B200_PREC_FFMA, s));
+}
+
+cudaError_t compute_rms_norm(Tensor *dst, cudaStream_t s) {
+    const Tensor *x = dst->src[0], *gamma = dst->src[1];
+    float eps = 0.f;
+    std::memcpy(&eps, &dst->op_params[0], sizeof eps);
+    return as_cuda(b200_rms_norm(cf(x), cf(gamma), mf(dst), x->dims[0], x->dims[1] * x->dims[2] * x->dims[3], eps, s));
+}
+
+cudaError_t compute_rope(Tensor *dst, cudaStream_t s) {
+    const Tensor *x = dst->src[0], *pos = dst->src[1], *tab = dst->src[2];
+    return as_cuda(b200_rope(cf(x), static_cast<const int32_t *>(pos->data), cf(tab), tab->dims[1], mf(dst),
+                             x->dims[0], x->dims[1], x->dims[2], nullptr, s));
+}
+
+cudaError_t compute_flash_attn(Tensor *dst, cudaStream_t s) {
+    const Tensor *q = dst->src[0], *k = dst->src[1], *v = dst->src[2];
+    AttnParams p{};
+    std::memcpy(&p, dst->op_params, sizeof p);
+    const int64_t D = q->dims[0];
+    const float scale = p.scale > 0.0f ? p.scale : 1.0f / std::sqrt(static_cast<float>(D));
+    // K / V are views of the cache: token stride strides[2], head stride strides[1] (bytes)
+    return as_cuda(b200_flash_attn(cf(q), cf(k), cf(v), mf(dst), D, q->dims[1], k->dims[1], q->dims[2], k->dims[2],
+                                   static_cast<int64_t>(p.n_ctx), scale, k->strides[2] / 4, k->strides[1] / 4,
+                                   v->strides[2] / 4, v->strides[1] / 4, nullptr, 0, s));
+}
+
+cudaError_t compute_get_rows(Tensor *dst, cudaStream_t s) {
+    const Tensor *table = dst->src[0], *ids = dst->src[1];
+    return as_cuda(b200_get_rows(cf(table), static_cast<const int32_t *>(ids->data), mf(dst), table->dims[0],
+                                 ids->dims[0], table->dims[1], nullptr, s));
+}
+
+cudaError_t compute_silu(Tensor *dst, cudaStream_t s) {
+    return as_cuda(b200_silu(cf(dst->src[0]), mf(dst), static_cast<int64_t>(dst->element_count()), s));
+}
+
+cudaError_t compute_mul(Tensor *dst, cudaStream_t s) {
+    return as_cuda(b200_mul(cf(dst->src[0]), cf(dst->src[1]), mf(dst), static_cast<int64_t>(dst->element_count()), s));
+}
+
+cudaError_t compute_add(Tensor *dst, cudaStream_t s) {
+    return as_cuda(b200_add(cf(dst->src[0]), cf(dst->src[1]), mf(dst), static_cast<int64_t>(dst->element_count()), s));
+}
+
+cudaError_t compute_cpy(Tensor *dst, cudaStream_t s) {
+    const Tensor *src = dst->src[0];
+    if (src->dataType != dst->dataType || src->dims != dst->dims) return cudaErrorInvalidValue;
+    return as_cuda(b200_copy(dst->data, src->data, src->byte_size(), s));
+}
+
+cudaError_t compute_reshape(Tensor *dst, cudaStream_t s) {
+    const Tensor *src = dst->src[0];
+    if (src->dataType != dst->dataType || src->element_count() != dst->element_count()) return cudaErrorInvalidValue;
+    return as_cuda(b200_copy(dst->data, src->data, src->byte_size(), s));
+}
+
+cudaError_t compute_view(Tensor *, cudaStream_t) { return cudaSuccess; }
+
+}  // namespace CUDA_F32

@@ -23,6 +23,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_LIB = os.path.join(HERE, "_build", "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libinferllm_ref.so")
+# the reference engine on its own CUDA backend with the B200 kernels swapped in
+# (oracle/Makefile `ref-b200`): the drop-in check, not a checker
+REF_B200_LIB = os.path.join(HERE, "_ref", "libinferllm_ref_b200.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
@@ -219,6 +222,8 @@ class Ref:
         L.ref_sample_greedy.restype = C.c_int32
         L.ref_engine_create.argtypes = [C.c_char_p, C.c_int, _i64]
         L.ref_engine_create.restype = C.c_void_p
+        L.ref_engine_create_cuda.argtypes = [C.c_char_p, C.c_int, _i64, C.c_int]
+        L.ref_engine_create_cuda.restype = C.c_void_p
         L.ref_engine_destroy.argtypes = [C.c_void_p]
         L.ref_engine_reset.argtypes = [C.c_void_p]
         L.ref_engine_reset.restype = C.c_int
@@ -306,9 +311,15 @@ class Ref:
 class RefEngine:
     """The reference end-to-end CPU path over a GGUF file (bench.cpp Runner)."""
 
-    def __init__(self, ref: Ref, gguf_path: str, threads: int, capacity: int):
+    def __init__(self, ref: Ref, gguf_path: str, threads: int, capacity: int, cuda_device: int | None = None):
+        """cuda_device selects the reference CUDA backend (layers and KV cache on that
+        device, embedding on the CPU, as benchmarks/cuda/bench.cpp:146-160 places them);
+        only a library built by `make ref-b200` has it."""
         self.ref = ref
-        self.h = ref.lib.ref_engine_create(gguf_path.encode(), threads, capacity)
+        if cuda_device is None:
+            self.h = ref.lib.ref_engine_create(gguf_path.encode(), threads, capacity)
+        else:
+            self.h = ref.lib.ref_engine_create_cuda(gguf_path.encode(), threads, capacity, cuda_device)
         if not self.h:
             raise RuntimeError("ref_engine_create failed")
 

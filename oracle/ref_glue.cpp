@@ -9,6 +9,13 @@
 //     Scheduler::execute, read_logits and the greedy Sampler, with the request
 //     loop of benchmarks/cpu/bench.cpp (Runner::evaluate, bench.cpp:177-219).
 // Nothing in the product library links or calls this file.
+//
+// Built with INFERLLM_WITH_CUDA (oracle/Makefile `ref-b200`), the same glue also
+// creates the reference engine on its own CUDA backend (cuda_backend.cpp) whose
+// CUDA_F32::compute_* kernels are the B200 library's (infer-llm_b200/integration/
+// kernel_b200.cpp): the reference host code driving the product, end to end, as the
+// drop-in check. Device placement follows benchmarks/cuda/bench.cpp:146-160,397-410
+// (layers and KV on cuda:<d>, embedding on the CPU, synchronize after each step).
 
 #include "backend.hpp"
 #include "backends/cpu_backend.hpp"
@@ -22,6 +29,9 @@
 #include "kvcache/KVStorages/naiveKVStorage.hpp"
 #include "kvcache/KVStrategys/contiguousKVStrategy.hpp"
 
+#ifdef INFERLLM_WITH_CUDA
+#include <cuda_runtime_api.h>
+#endif
 #include <cstdlib>
 #include <cstring>
 #include <iostream>
@@ -201,6 +211,7 @@ int32_t ref_sample_greedy(const float *logits, int64_t n) {
 // End-to-end reference CPU engine (one sequence at a time).
 
 struct RefEngine {
+    std::unique_ptr<Backend> gpu;  // the reference CUDA backend, or null (CPU engine)
     std::unique_ptr<ModelBase> model;
     std::unique_ptr<KVCacheManager> cache;
     std::unique_ptr<GraphContext> ctx;
@@ -212,10 +223,17 @@ struct RefEngine {
     int64_t n_vocab = 0;
 };
 
-void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
+static void *engine_create(const char *gguf_path, int threads, int64_t capacity, int cuda_device) {
     Backend *b = cpu_backend(threads);
     if (!b) return nullptr;
     Quiet q;
+    std::unique_ptr<Backend> gpu;
+    if (cuda_device >= 0) {
+        auto g = BackendRegistry::instance().create("cuda:" + std::to_string(cuda_device), PoolConfig{});
+        if (!g) return nullptr;
+        gpu = std::move(*g);
+    }
+    Backend *dev = gpu ? gpu.get() : b;  // where the layers and the KV cache live
     auto gguf = GGUFContext::load(gguf_path);
     if (!gguf) return nullptr;
     auto arch = gguf->metadata().get_meta<std::string>("general.architecture");
@@ -231,11 +249,12 @@ void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
         models_registered = true;
     }
     auto e = std::make_unique<RefEngine>();
+    e->gpu = std::move(gpu);
     auto model = ModelBase::load_model(std::move(*gguf));
     if (!model) return nullptr;
     e->model = std::move(*model);
     if (!e->model->load_hparams() || !e->model->load_weight()) return nullptr;
-    e->devices = {b};
+    e->devices = e->gpu ? std::vector<Backend *>{dev, b} : std::vector<Backend *>{b};
     PlacementConfig placement;
     placement.n_ctx = static_cast<uint32_t>(capacity);
     if (!e->model->plan_weights_placement(e->devices, placement)) return nullptr;
@@ -246,7 +265,7 @@ void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
                                                            .v_type = GGML_TYPE_F32});
     e->cache = std::make_unique<KVCacheManager>(
         std::make_unique<ContiguousKVStrategy>(std::make_unique<NaiveKVStorage>()));
-    std::vector<Backend *> placement_layers(layers.size(), b);
+    std::vector<Backend *> placement_layers(layers.size(), dev);
     KVCacheConfig config{.layers = layers.size(), .max_tokens_per_sequence = static_cast<size_t>(capacity)};
     if (!e->cache->init(layers, placement_layers, config)) return nullptr;
     e->ctx = std::make_unique<GraphContext>(b);
@@ -265,6 +284,20 @@ void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
     e->seq = *seq;
     if (!e->ctx->set_kv_cache(e->cache.get(), e->seq)) return nullptr;
     return e.release();
+}
+
+void *ref_engine_create(const char *gguf_path, int threads, int64_t capacity) {
+    return engine_create(gguf_path, threads, capacity, -1);
+}
+
+// The reference engine on its CUDA backend (null unless built with INFERLLM_WITH_CUDA).
+void *ref_engine_create_cuda(const char *gguf_path, int threads, int64_t capacity, int device) {
+#ifdef INFERLLM_WITH_CUDA
+    return engine_create(gguf_path, threads, capacity, device);
+#else
+    (void)gguf_path, (void)threads, (void)capacity, (void)device;
+    return nullptr;
+#endif
 }
 
 void ref_engine_destroy(void *h) {
@@ -315,6 +348,9 @@ int32_t ref_engine_eval(void *h, const int32_t *ids, int64_t n, float *last_logi
         if (!graph) goto fail;
         if (!graph->compute()) goto fail;
         if (!e->scheduler->execute(*graph)) goto fail;
+#ifdef INFERLLM_WITH_CUDA
+        if (e->gpu && cudaDeviceSynchronize() != cudaSuccess) goto fail;  // bench.cpp:210-213
+#endif
         auto logits = read_logits(*graph->outputs().front(), static_cast<size_t>(n - 1));
         if (!logits) goto fail;
         if (last_logits) std::memcpy(last_logits, logits->data(), sizeof(float) * logits->size());
