@@ -73,6 +73,15 @@ B200_DEVICE uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 16-byte shared-memory load at a 32-bit shared address (an explicit ld.shared:
+// generic loads of shared data through pointers kept in structs cost a
+// generic-to-shared resolution each).
+B200_DEVICE float4 lds4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
 B200_DEVICE void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
                  : "memory");

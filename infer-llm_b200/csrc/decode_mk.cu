@@ -48,6 +48,7 @@ constexpr int kMaxRpc = 8;           // rows per ring chunk at most
 constexpr int kMaxK = 3072;          // largest projection input (= one ring stage)
 constexpr int kMaxLayers = 40;
 constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
+constexpr int kResFloats = 64;       // this CTA's rows of the residual stream
 constexpr int kMaxSplits = 18;
 constexpr int kDefaultInflight = 8;  // measured: 8 copies (96 KB) per SM keep HBM busy; 3 starve the LM head
 constexpr int kMaxGq = 4;            // query heads per KV head (attention registers)
@@ -211,11 +212,6 @@ B200_DEVICE void st_tagged(u64 *p, float v, uint32_t tag) {
 B200_DEVICE void ld_tagged2(const u64 *p, u64 &a, u64 &b) {
     asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-B200_DEVICE u64 ld_tagged1(const u64 *p) {
-    u64 a;
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
-    return a;
-}
 
 // Polls word pairs until both carry `tag`: `pending` is a bit mask over the
 // caller's pairs, `reload(j)` re-reads pair j. Gives up (status set) after
@@ -255,6 +251,7 @@ struct Smem {
     float *xs;     // [kMaxK] phase input activation
     float *part;   // [kPartFloats]
     float *qs;     // [Gq][D] rotated queries of the KV group (attention)
+    float *res;    // [kResFloats] this CTA's residual rows (o_proj / down row range)
 };
 
 template <int D>
@@ -388,20 +385,21 @@ struct Mk {
     // so no FMA waits on the previous one; then reduces the R row sums across the
     // warp (fixed order) into dst[0..R).
     template <int R>
-    B200_DEVICE void chunk_rows(const float4 *w4, const float4 *x4, int64_t K4, float *dst) {
+    B200_DEVICE void chunk_rows(uint32_t w_sa, uint32_t x_sa, int K4, float *dst) {
         constexpr int U = R == 1 ? 8 : (R <= 3 ? 4 : 2);
         float4 a[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) a[r] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-        for (int64_t i0 = lane; i0 < K4; i0 += 32 * U) {
+        for (int i0 = lane; i0 < K4; i0 += 32 * U) {
             float4 xv[U], wv[R][U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int64_t i = i0 + 32 * u;
-                xv[u] = i < K4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int i = i0 + 32 * u;
+                xv[u] = i < K4 ? lds4(x_sa + 16u * i) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int r = 0; r < R; ++r) wv[r][u] = i < K4 ? w4[r * K4 + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < R; ++r)
+                    wv[r][u] = i < K4 ? lds4(w_sa + 16u * (r * K4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
@@ -438,9 +436,9 @@ struct Mk {
         uint64_t t_wait = 0;
         const long long tl0 = tr ? clock64() : 0;
         const int rpc = rpc_for(pw.K, pw.unit);
-        const int64_t K4 = pw.K >> 2;
+        const int K4 = static_cast<int>(pw.K >> 2);
         const int64_t nch = (r1 - r0 + rpc - 1) / rpc;
-        const float4 *x4 = reinterpret_cast<const float4 *>(sm.xs);
+        const uint32_t x_sa = smem_addr(sm.xs);
         __shared__ int s_fail;
         if (tid == 0) s_fail = 0;
         named_sync(1, kCT);
@@ -456,17 +454,18 @@ struct Mk {
             if (tr) t_wait += clock64() - tw0;
             const int64_t row = r0 + k * rpc;
             const int rows = static_cast<int>(min64(rpc, r1 - row));
-            const float4 *w4 = reinterpret_cast<const float4 *>(sm.ring + static_cast<size_t>(s) * kStageFloats);
+            const uint32_t w_sa = smem_addr(sm.ring) + 4u * kStageFloats * s;
             float *dst = sm.part + (row - r0);
 #pragma unroll 1
             for (int r = 0; r < rows; r += 3) {  // sub-chunks of at most 3 rows
                 const int n = min(3, rows - r);
+                const uint32_t wr_sa = w_sa + 16u * r * K4;
                 if (n == 3)
-                    chunk_rows<3>(w4 + r * K4, x4, K4, dst + r);
+                    chunk_rows<3>(wr_sa, x_sa, K4, dst + r);
                 else if (n == 2)
-                    chunk_rows<2>(w4 + r * K4, x4, K4, dst + r);
+                    chunk_rows<2>(wr_sa, x_sa, K4, dst + r);
                 else
-                    chunk_rows<1>(w4 + r * K4, x4, K4, dst + r);
+                    chunk_rows<1>(wr_sa, x_sa, K4, dst + r);
             }
             __syncwarp();  // the stage is read: hand it back to the producer
             if (lane == 0) mbar_arrive(&sm.empty[s]);
@@ -723,11 +722,13 @@ struct Mk {
     }
 
     // ---- o_proj input: merge the attention splits (split order) into xs. Every
-    // split's (m, l) first, then per thread its word pairs of up to kSG splits'
-    // partial outputs in flight together.
+    // split's (m, l) and the first kSG splits' partial outputs are requested
+    // together (one L2 round trip for S <= kSG), the split weights are formed from
+    // (m, l), then per thread its word pairs of the next kSG splits at a time.
     B200_DEVICE bool merge_attention(int layer, int64_t n_past) {
         constexpr int kP = 4;   // word pairs per thread: Hq * D <= 2 * kP * kCT
         constexpr int kSG = 2;  // splits loaded per round (register budget)
+        constexpr int kM = 2;   // (split, head) pairs per thread: kMaxSplits * Hq <= kM * kCT
         const uint32_t want = tag(layer, PH_ATTN);
         const int S = attn_splits(n_past + 1);
         const int Hq = p.Hq;
@@ -738,9 +739,23 @@ struct Mk {
         __shared__ int s_bad;
         if (tid == 0) s_bad = 0;
         named_sync(1, kCT);
+        u64 oa[kSG * kP], oc[kSG * kP];  // one round of partial-output pairs
+        unsigned opend = 0;
+        auto issue = [&](int s0) {
+            opend = 0;
+#pragma unroll
+            for (int j = 0; j < kSG; ++j)
+#pragma unroll
+                for (int v = 0; v < kP; ++v) {
+                    const int i2 = tid + v * kCT;
+                    if (s0 + j < S && i2 < n2) {
+                        ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + i2) * 2, oa[j * kP + v], oc[j * kP + v]);
+                        opend |= 1u << (j * kP + v);
+                    }
+                }
+        };
         bool ok = true;
         {
-            constexpr int kM = 2;  // (split, head) pairs per thread: kMaxSplits * Hq <= kM * kCT
             u64 a[kM], c[kM];
             unsigned pending = 0;
 #pragma unroll
@@ -751,6 +766,7 @@ struct Mk {
                     pending |= 1u << j;
                 }
             }
+            issue(0);  // in flight while (m, l) is polled and the weights are formed
             ok = poll_pairs<kM>(
                 pending, p.status, p.status, [&](int j) { return tag_hi(a[j]) == want && tag_hi(c[j]) == want; },
                 [&](int j) { ld_tagged2(p.tpml + 2 * (tid + j * kCT), a[j], c[j]); });
@@ -785,24 +801,13 @@ struct Mk {
         for (int v = 0; v < kP; ++v) acc[v] = make_float2(0.f, 0.f);
 #pragma unroll 1
         for (int s0 = 0; s0 < S && ok; s0 += kSG) {
-            u64 a[kSG * kP], c[kSG * kP];
-            unsigned pending = 0;
-#pragma unroll
-            for (int j = 0; j < kSG; ++j)
-#pragma unroll
-                for (int v = 0; v < kP; ++v) {
-                    const int i2 = tid + v * kCT;
-                    if (s0 + j < S && i2 < n2) {
-                        ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + i2) * 2, a[j * kP + v], c[j * kP + v]);
-                        pending |= 1u << (j * kP + v);
-                    }
-                }
+            if (s0) issue(s0);
             ok = poll_pairs<kSG * kP>(
-                pending, p.status, p.status,
-                [&](int q) { return tag_hi(a[q]) == want && tag_hi(c[q]) == want; },
+                opend, p.status, p.status,
+                [&](int q) { return tag_hi(oa[q]) == want && tag_hi(oc[q]) == want; },
                 [&](int q) {
                     const int j = q / kP, v = q % kP;
-                    ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + tid + v * kCT) * 2, a[q], c[q]);
+                    ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + tid + v * kCT) * 2, oa[q], oc[q]);
                 });
 #pragma unroll
             for (int j = 0; j < kSG; ++j)
@@ -811,8 +816,8 @@ struct Mk {
                     const int i2 = tid + v * kCT;
                     if (s0 + j < S && i2 < n2) {
                         const float f = sw[(s0 + j) * Hq + i2 * 2 / D];
-                        acc[v].x = fmaf(f, tag_val(a[j * kP + v]), acc[v].x);
-                        acc[v].y = fmaf(f, tag_val(c[j * kP + v]), acc[v].y);
+                        acc[v].x = fmaf(f, tag_val(oa[j * kP + v]), acc[v].x);
+                        acc[v].y = fmaf(f, tag_val(oc[j * kP + v]), acc[v].y);
                     }
                 }
         }
@@ -888,6 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
     sm.xs = sm.ring + kStages * kStageFloats;
     sm.part = sm.xs + kMaxK;
     sm.qs = sm.part + kPartFloats;
+    sm.res = sm.qs + kMaxGq * D;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x, G = gridDim.x;
@@ -938,6 +944,13 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
     }
     const float *emb = p.tok_embd + static_cast<int64_t>(ok ? token : 0) * p.H;
     int64_t r0 = 0, r1 = 0;
+    {
+        // The o_proj and down phases own the same H rows per CTA: their residual
+        // stays in shared memory from phase to phase (layer 0: the embedding).
+        rows_of(p.H, 1, b, G, r0, r1);
+#pragma unroll 1
+        for (int64_t r = r0 + tid; r < r1; r += kCT) mk.sm.res[r - r0] = __ldg(emb + r);
+    }
     // One pass over the step's phases (per layer QKV, attention, o_proj, gate/up,
     // down; then the LM head), each helper called from exactly one place so that
     // the kernel's code stays small enough for the instruction cache.
@@ -985,8 +998,10 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
 #pragma unroll 1
             for (int64_t r = r0 + tid; r < r1; r += kCT) {
                 float v = mk.row_sum(r - r0);
-                if (ph != PH_QKV)  // residual: this CTA's own earlier rows (layer 0: the embedding)
-                    v += (ph == PH_O && l == 0) ? __ldg(emb + r) : tag_val(ld_tagged1(p.tx + r));
+                if (ph != PH_QKV) {  // residual: this CTA's own rows, kept in shared memory
+                    v += mk.sm.res[r - r0];
+                    mk.sm.res[r - r0] = v;
+                }
                 st_tagged(dst + r, v, mine);
             }
         }
@@ -1083,7 +1098,8 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
 
 size_t smem_bytes(int D) {
     return 256 + static_cast<size_t>(kStages) * kStageFloats * 4 + static_cast<size_t>(kMaxK) * 4 +
-           static_cast<size_t>(kPartFloats) * 4 + static_cast<size_t>(kMaxGq) * D * 4;
+           static_cast<size_t>(kPartFloats) * 4 + static_cast<size_t>(kMaxGq) * D * 4 +
+           static_cast<size_t>(kResFloats) * 4;
 }
 
 }  // namespace
@@ -1113,6 +1129,7 @@ bool mk_supported(const MkParams &p) {
     if (kCW * (p.Hq / p.Hkv) * (p.D + 2) > kMaxK + kPartFloats - 2 * p.D) return false;
     const int G = mk_grid();
     if (p.Hkv > G) return false;
+    if ((p.H + G - 1) / G > kResFloats) return false;  // residual rows per CTA
     // 32-bit row-range arithmetic (rows_of)
     const int64_t nmax = std::max<int64_t>({static_cast<int64_t>(p.V), 2 * static_cast<int64_t>(p.F),
                                             static_cast<int64_t>(p.Hq + 2 * p.Hkv) * p.D});
