@@ -391,6 +391,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         g.epi = GEMM_STORE;
         g.ws = e->gemm_ws;
         g.ws_floats = e->gemm_ws_floats;
+        g.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(g, st, pdl) : gemm_ffma_launch(g, st, pdl));
 
         QkNormRopeArgs r;
@@ -449,6 +450,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         o.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
         o.ws = e->gemm_ws;
         o.ws_floats = e->gemm_ws_floats;
+        o.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(o, st, pdl) : gemm_ffma_launch(o, st, pdl));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
 
@@ -465,6 +467,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         gu.epi = GEMM_SWIGLU;
         gu.ws = e->gemm_ws;
         gu.ws_floats = e->gemm_ws_floats;
+        gu.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(gu, st, pdl) : gemm_ffma_launch(gu, st, pdl));
 
         GemmArgs dn;
@@ -480,6 +483,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         dn.epi = (e->tp && e->c.tp_rank != 0) ? GEMM_STORE : GEMM_RESIDUAL;
         dn.ws = e->gemm_ws;
         dn.ws_floats = e->gemm_ws_floats;
+        dn.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(dn, st, pdl) : gemm_ffma_launch(dn, st, pdl));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
     }

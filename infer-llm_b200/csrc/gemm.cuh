@@ -26,12 +26,18 @@ struct GemmArgs {
     float *ws = nullptr;
     int64_t ws_floats = 0;
     int64_t k_split = 0;  // set by the launcher: K per split (0 = no split)
+    int32_t *status = nullptr;  // device status word for bounded-wait timeouts (tcgen05 GEMM)
 };
 
 // Exact F32 FFMA tiled GEMM (any M; K % 4 == 0).
 cudaError_t gemm_ffma_launch(const GemmArgs &a, cudaStream_t stream, bool pdl);
-// tcgen05 TF32 tensor-core GEMM (TMEM accumulators, bulk-staged operands).
-// Returns cudaErrorNotSupported for shapes it does not cover.
+// tcgen05 TF32 tensor-core GEMM (TMA-staged 128-byte-swizzled operands, TMEM
+// accumulators). Returns cudaErrorNotSupported for operands TMA cannot describe
+// (unaligned bases or strides).
 cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl);
+// Sums a.ws[0..splits) (split-K partials, [M][N] each) in split order and applies
+// a.epi into a.c.
+cudaError_t gemm_splitk_reduce_launch(const GemmArgs &a, int splits, cudaStream_t stream, bool pdl);
+int device_sm_count();
 
 }  // namespace b200

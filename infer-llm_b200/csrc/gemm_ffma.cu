@@ -234,16 +234,7 @@ cudaError_t launch_bm(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
     if (a.k_split) {
         cudaError_t e = b200_launch(sgemm_kernel<BM, GEMM_STORE>, grid, dim3(NT), 0, stream, pdl, a);
         if (e != cudaSuccess) return e;
-        const int splits = static_cast<int>(grid.z);
-        const int64_t outs = a.M * (a.epi == GEMM_SWIGLU ? a.N / 2 : a.N);
-        const dim3 rg(static_cast<unsigned>((outs + 255) / 256));
-        switch (a.epi) {
-            case GEMM_STORE: return b200_launch(splitk_reduce_kernel<GEMM_STORE>, rg, dim3(256), 0, stream, pdl, a, splits);
-            case GEMM_RESIDUAL:
-                return b200_launch(splitk_reduce_kernel<GEMM_RESIDUAL>, rg, dim3(256), 0, stream, pdl, a, splits);
-            case GEMM_SWIGLU: return b200_launch(splitk_reduce_kernel<GEMM_SWIGLU>, rg, dim3(256), 0, stream, pdl, a, splits);
-        }
-        return cudaErrorInvalidValue;
+        return gemm_splitk_reduce_launch(a, static_cast<int>(grid.z), stream, pdl);
     }
     switch (a.epi) {
         case GEMM_STORE: return b200_launch(sgemm_kernel<BM, GEMM_STORE>, grid, dim3(NT), 0, stream, pdl, a);
@@ -254,6 +245,18 @@ cudaError_t launch_bm(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
 }
 
 }  // namespace
+
+cudaError_t gemm_splitk_reduce_launch(const GemmArgs &a, int splits, cudaStream_t stream, bool pdl) {
+    const int64_t outs = a.M * (a.epi == GEMM_SWIGLU ? a.N / 2 : a.N);
+    const dim3 rg(static_cast<unsigned>((outs + 255) / 256));
+    switch (a.epi) {
+        case GEMM_STORE: return b200_launch(splitk_reduce_kernel<GEMM_STORE>, rg, dim3(256), 0, stream, pdl, a, splits);
+        case GEMM_RESIDUAL:
+            return b200_launch(splitk_reduce_kernel<GEMM_RESIDUAL>, rg, dim3(256), 0, stream, pdl, a, splits);
+        case GEMM_SWIGLU: return b200_launch(splitk_reduce_kernel<GEMM_SWIGLU>, rg, dim3(256), 0, stream, pdl, a, splits);
+    }
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t gemm_ffma_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0 || (a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;

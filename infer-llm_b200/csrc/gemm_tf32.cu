@@ -1,7 +1,331 @@
-// Placeholder until the tcgen05 TF32 GEMM lands: the engine and b200_mul_mat
-// treat cudaErrorNotSupported as "use the FFMA GEMM".
+// Prefill matrix products on the 5th-generation tensor cores (tcgen05, kind::tf32):
+// C[M][N] = X[M][K] . W[N][K]^T with the STORE / RESIDUAL / SWIGLU epilogues of the
+// FFMA GEMM (gemm_ffma.cu), for B200_PREC_TF32.
+//
+// One CTA computes one 128 x 128 tile of C (split over K when the tile grid
+// leaves SMs idle). Both operands are K-major in HBM (X rows are tokens, W rows
+// are output features), which is the layout tcgen05 reads directly:
+//   * warp 0, one lane: TMA engine. 2-D tiled copies (cuTensorMapEncodeTiled,
+//     128-byte swizzle) of a [128 rows x 32 floats] box of X and of W per stage
+//     into a kTStages-deep shared-memory ring, completing on the stage's mbarrier;
+//   * warp 1, one lane: tensor cores. Per stage four tcgen05.mma (M 128, N 128,
+//     K 8 each) from shared-memory descriptors into a 128-column F32
+//     accumulator in tensor memory; tcgen05.commit hands the stage back to the
+//     copy engine once the MMAs that read it are done, and a final commit
+//     signals the epilogue;
+//   * all four warps: epilogue. Warp w reads TMEM lanes 32w..32w+31 (= tile rows)
+//     with tcgen05.ld, 16 columns at a time, and writes C (or split-K partials).
+// TF32 multiplies use the top 19 bits of each F32 operand and accumulate in F32,
+// so results differ from the exact F32 reference by ~1e-3 relative (the
+// B200_PREC_TF32 tolerance); B200_PREC_FFMA is the exact path.
+//
+// Every mbarrier wait is bounded: a wait that runs out records B200_DEV_TIMEOUT in
+// the status word, skips the remaining work, waits (bounded) for this CTA's copies
+// in flight and frees its tensor memory before returning.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "gemm.cuh"
 
 namespace b200 {
-cudaError_t gemm_tf32_launch(const GemmArgs &, cudaStream_t, bool) { return cudaErrorNotSupported; }
+namespace {
+
+constexpr int kTBM = 128, kTBN = 128, kTBK = 32;  // kTBK floats = one 128-byte swizzle row
+constexpr int kTStages = 5;
+constexpr uint32_t kTileBytes = kTBM * kTBK * 4;  // 16 KB per operand per stage (kTBM == kTBN)
+constexpr uint32_t kStageBytes = 2 * kTileBytes;
+constexpr int kTThreads = 128;
+constexpr uint32_t kTmemCols = 128;  // F32 accumulator: 128 lanes x kTBN columns
+static_assert(kTBM == kTBN, "one box shape for both operands");
+static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocations are powers of two >= 32");
+
+constexpr size_t kTSmem = 1024 /* alignment slack */ + static_cast<size_t>(kTStages) * kStageBytes + 256;
+
+// Instruction descriptor of kind::tf32: F32 accumulate (bits 4-5 = 1), A and B TF32
+// (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22,
+// M >> 4 at bits 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kTBN >> 3) << 17) |
+                            (static_cast<uint32_t>(kTBM >> 4) << 24);
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with the
+// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte
+// offset), leading byte offset unused (1), descriptor version 1, layout SWIZZLE_128B
+// (2 at bits 61-63). The tile base is 1024-byte aligned; stepping K by 8 TF32
+// elements inside the 128-byte row advances the start address by 32 bytes.
+B200_DEVICE uint64_t desc_k_sw128(uint32_t saddr) {
+    uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+B200_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+B200_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+B200_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+B200_DEVICE void tc_mma_tf32(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued so far has completed.
+B200_DEVICE void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns of tensor memory (thread t: lane t).
+B200_DEVICE void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Bounded mbarrier wait (hardware-suspended polls); false and B200_DEV_TIMEOUT
+// after ~2 s, or at once if another CTA already reported an error.
+B200_DEVICE bool wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 7) == 7) {
+            if (status && *reinterpret_cast<volatile int32_t *>(status)) return false;
+            if (global_ns() - t0 > 2000000000ull) break;
+        }
+    }
+    set_status(status, B200_DEV_TIMEOUT);
+    return false;
+}
+
+__device__ int32_t g_tf32_status;  // status word when the caller passes none
+
+template <int EPI>
+__global__ void __launch_bounds__(kTThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const GemmArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
+    unsigned char *gbase = smem_raw + (sbase - raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(gbase + kTStages * kStageBytes);
+    uint64_t *empty = full + kTStages;
+    uint64_t *done = empty + kTStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    int32_t *status = a.status ? a.status : &g_tf32_status;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTBM, n0 = static_cast<int64_t>(blockIdx.x) * kTBN;
+    const int64_t kbeg = a.k_split ? static_cast<int64_t>(blockIdx.z) * a.k_split : 0;
+    const int64_t kend = a.k_split ? min64(a.K, kbeg + a.k_split) : a.K;
+    const int nk = static_cast<int>((kend - kbeg + kTBK - 1) / kTBK);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmx)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
+    }
+    if (warp == 2) {  // one warp owns the tensor-memory allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    grid_launch_dependents();
+    grid_wait();  // X (and the residual) come from the previous kernel
+
+    if (warp == 0 && lane == 0) {
+        // ---- copy engine: stage s of k-step kt, after the MMAs of k-step kt - kTStages released it
+        int issued = 0;
+#pragma unroll 1
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kTStages;
+            if (kt >= kTStages && !wait_bounded(&empty[s], ((kt / kTStages) - 1) & 1, status)) break;
+            const uint32_t dst = sbase + s * kStageBytes;
+            const int32_t kx = static_cast<int32_t>(kbeg + static_cast<int64_t>(kt) * kTBK);
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(dst, &tmx, kx, static_cast<int32_t>(m0), smem_addr(&full[s]));
+            tma_load_2d(dst + kTileBytes, &tmw, kx, static_cast<int32_t>(n0), smem_addr(&full[s]));
+            ++issued;
+        }
+        // copies still landing in this CTA's shared memory: the last kTStages issued
+#pragma unroll 1
+        for (int kt = issued > kTStages ? issued - kTStages : 0; kt < issued; ++kt)
+            wait_bounded(&full[kt % kTStages], (kt / kTStages) & 1, nullptr);
+    } else if (warp == 1 && lane == 0) {
+        // ---- tensor cores
+#pragma unroll 1
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kTStages;
+            if (!wait_bounded(&full[s], (kt / kTStages) & 1, status)) break;
+            tc_fence_after();
+            const uint64_t da = desc_k_sw128(sbase + s * kStageBytes);
+            const uint64_t db = desc_k_sw128(sbase + s * kStageBytes + kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < kTBK / 8; ++kk)  // K 8 per MMA: +32 bytes = +2 in the address field
+                tc_mma_tf32(tmem, da + 2 * kk, db + 2 * kk, (kt | kk) != 0);
+            tc_commit(smem_addr(&empty[s]));
+        }
+        tc_commit(smem_addr(done));  // the accumulator is complete (or nothing was issued)
+    }
+    __syncwarp();
+
+    // ---- epilogue: thread (warp w, lane t) owns tile row 32w + t
+    // warp-uniform: tcgen05.ld below is a warp-collective (.sync.aligned) instruction
+    const bool have = __all_sync(0xffffffffu, wait_bounded(done, 0, status)) && nk > 0;
+    tc_fence_after();
+    if (have) {
+        const int64_t gm = m0 + 32 * warp + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kTBN; c0 += 16) {
+            float v[16];
+            __syncwarp();
+            tc_ld16(trow + c0, v);  // warp-collective: every lane takes part
+            const int64_t gn = n0 + c0;
+            if (gm >= a.M || gn >= a.N) continue;
+            if (a.k_split) {  // raw partial sums of this split: ws[z][M][N]
+                float *ws = a.ws + static_cast<int64_t>(blockIdx.z) * a.M * a.N + gm * a.N;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (gn + j < a.N) ws[gn + j] = v[j];
+            } else if (EPI == GEMM_SWIGLU) {  // (gate, up) column pairs -> one output
+#pragma unroll
+                for (int j = 0; j < 16; j += 2)
+                    if (gn + j + 1 < a.N) {
+                        const float g = v[j], u = v[j + 1];
+                        const float sg = g / (1.0f + expf(-g));
+                        a.c[gm * a.ldc + (gn + j) / 2] = u * sg;
+                    }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (gn + j < a.N) {
+                        float o = v[j];
+                        if (EPI == GEMM_RESIDUAL) o = o + a.r[gm * a.ldc + gn + j];
+                        a.c[gm * a.ldc + gn + j] = o;
+                    }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// [rows][cols] F32 matrix with row stride `ld` floats, boxes of [128 rows x 32 floats].
+bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {kTBK, kTBM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a, dim3 grid, cudaStream_t st,
+                       bool pdl) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        const cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kTSmem));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    return b200_launch(gemm_tf32_kernel<EPI>, grid, dim3(kTThreads), kTSmem, st, pdl, mx, mw, a);
+}
+
+}  // namespace
+
+cudaError_t gemm_tf32_launch(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
+    GemmArgs a = a_in;
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
+    if (a.epi == GEMM_SWIGLU && (a.N & 1)) return cudaErrorInvalidValue;
+    // TMA: 16-byte aligned bases and row strides; the tile rows must fit 32-bit coordinates
+    if ((a.K & 3) || (a.ldx & 3) || (reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
+        a.M >= (int64_t(1) << 31) || a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 31))
+        return cudaErrorNotSupported;
+    CUtensorMap mx, mw;
+    if (!encode(&mx, a.x, a.M, a.K, a.ldx) || !encode(&mw, a.w, a.N, a.K, a.K)) return cudaErrorNotSupported;
+    dim3 grid(static_cast<unsigned>((a.N + kTBN - 1) / kTBN), static_cast<unsigned>((a.M + kTBM - 1) / kTBM));
+    // Split K when the tile grid leaves SMs idle (short prompts): about one CTA per
+    // SM, at least 256 of K per split, partials reduced in split order.
+    a.k_split = 0;
+    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y, target = device_sm_count();
+    if (a.ws && tiles < target && a.K >= 512) {
+        int64_t splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
+        while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
+        if (splits > 1) {
+            a.k_split = ((a.K + splits - 1) / splits + kTBK - 1) / kTBK * kTBK;
+            grid.z = static_cast<unsigned>((a.K + a.k_split - 1) / a.k_split);
+        }
+    }
+    if (a.k_split) {
+        const cudaError_t e = launch_epi<GEMM_STORE>(mx, mw, a, grid, stream, pdl);
+        if (e != cudaSuccess) return e;
+        return gemm_splitk_reduce_launch(a, static_cast<int>(grid.z), stream, pdl);
+    }
+    switch (a.epi) {
+        case GEMM_STORE: return launch_epi<GEMM_STORE>(mx, mw, a, grid, stream, pdl);
+        case GEMM_RESIDUAL: return launch_epi<GEMM_RESIDUAL>(mx, mw, a, grid, stream, pdl);
+        case GEMM_SWIGLU: return launch_epi<GEMM_SWIGLU>(mx, mw, a, grid, stream, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace b200

@@ -1,0 +1,118 @@
+"""The tcgen05 TF32 prefill GEMM (B200_PREC_TF32) and the engine on it.
+
+Op level: C = X . W^T through b200_mul_mat with precision TF32, against
+  (1) the product of the TF32-rounded operands in float64: the tensor cores read
+      the top 19 bits of each F32 operand (sign, 8 exponent, 10 mantissa bits) and
+      accumulate in F32, so the result must equal that product up to F32
+      accumulation error (<= 5e-5 of the output RMS for K up to 3072);
+  (2) the exact F32 product (the reference's own definition of mul_mat,
+      kernel_f32.cu:180-205): within 4e-3 max error relative to |want| + RMS, the
+      stated op-level TF32 bound.
+Both operand roundings (toward zero, and to nearest) are emulated; the kernel must
+match one of them.
+Engine level (the 2e-3 logit bound): max |logit - want| <= 2e-3 x max |want|, and
+the greedy tokens are identical. The tensor cores truncate each operand to TF32
+(round toward zero, measured: the op-level result matches the truncated-operand
+product, not the rounded one), so every product is biased low by ~3.5e-4 per
+operand and the error compounds over the layers; relative to the logit RMS it is
+~7e-3 on the Qwen3-0.6B shape, relative to the largest logit ~1.6e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+import b200infer as B
+from b200infer import gguf as G
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def tf32(a, mode):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    if mode == "rn":  # round half away from zero on the 13 dropped bits
+        u = u + 0x1000
+    return (u & 0xFFFFE000).astype(np.uint32).view(np.float32)
+
+
+def rms(a):
+    return float(np.sqrt(np.mean(np.asarray(a, np.float64) ** 2))) + 1e-30
+
+
+def logit_err(got, want):
+    """max |got - want| / max |want|: error on the scale of the logits."""
+    want = np.asarray(want, np.float64)
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / np.max(np.abs(want)))
+
+
+SHAPES = [  # (M, N, K): prompt rows x output features x inner size
+    (32, 4096, 1024),    # QKV of a 32-token prompt (split K)
+    (128, 1024, 2048),   # o_proj
+    (200, 6144, 1024),   # gate/up, ragged M
+    (64, 1024, 3072),    # down
+    (130, 264, 1056),    # ragged N and M, K not a multiple of 128
+    (5, 8, 64),          # one tile, mostly padding
+    (257, 136, 1028),    # K % 32 == 4: zero-filled K tail
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_mul_mat_tf32(cuda, M, N, K):
+    rng = np.random.default_rng(M * 131 + N * 7 + K)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    got = B.mul_mat(torch.from_numpy(w).to(cuda), torch.from_numpy(x).to(cuda), precision=B.PREC_TF32).cpu().numpy()
+    exact = x.astype(np.float64) @ w.astype(np.float64).T
+    emu = {m: tf32(x, m).astype(np.float64) @ tf32(w, m).astype(np.float64).T for m in ("rz", "rn")}
+    e_emu = min(float(np.max(np.abs(got - e))) / rms(e) for e in emu.values())
+    assert np.all(np.isfinite(got))
+    assert e_emu <= 5e-5, f"vs TF32-operand product: {e_emu:.3g}"
+    assert rel_err(got, exact) <= 4e-3
+
+
+def test_tf32_engine_matches_golden(cuda, golden, tmp_path):
+    cfg = G.QWEN3_TINY
+    path = str(tmp_path / "tiny.gguf")
+    G.write_gguf(path, cfg, seed=7)
+    eng = B.Engine(cfg, kv_capacity=64, max_batch=16, precision=B.PREC_TF32).load_gguf(path).finalize()
+    logits = np.empty(cfg.n_vocab, np.float32)
+    tok = eng.eval(golden["e2e_prompt"], logits)
+    assert logit_err(logits, golden["e2e_logits_prefill"]) <= 2e-3
+    ref = [int(t) for t in golden["e2e_tokens"]]
+    toks = [tok]
+    for i in range(15):
+        toks.append(eng.eval(np.array([ref[i]], np.int32), logits))
+    assert toks == ref
+    # a second prefill after decodes (uneven batch, K/V appended at n_past)
+    eng.eval(np.array([3, 4, 5, 6, 7, 8, 9], np.int32), logits)
+    assert np.all(np.isfinite(logits))
+    eng.close()
+
+
+@pytest.mark.parametrize("plen", [32, 160])
+def test_tf32_qwen3_06b_prefill(cuda, port, plen):
+    """Qwen3-0.6B shape with TF32 prefill GEMMs (split K across the SMs for these
+    prompt lengths): prefill logits within the 2e-3 logit bound of the exact
+    restatement, greedy tokens identical at every teacher-forced decode step."""
+    import os
+    import oracle
+    threads = os.cpu_count() or 4
+    cfg = G.QWEN3_0_6B
+    path = G.cached_model(cfg, seed=0)
+    rd = G.GGUFReader(path)
+    pm = oracle.PortQwen3(port, cfg.as_dict(), {n: rd.tensor(n) for n in rd.names()}, kv_capacity=plen + 16)
+    eng = B.Engine(cfg, kv_capacity=plen + 16, max_batch=plen, precision=B.PREC_TF32).load_gguf(path).finalize()
+    prompt = np.random.default_rng(plen).integers(0, cfg.n_vocab, plen).astype(np.int32)
+    lg = np.empty(cfg.n_vocab, np.float32)
+    tok = eng.eval(prompt, lg)
+    want = pm.eval(prompt, threads=threads)[0]
+    assert logit_err(lg, want) <= 2e-3
+    ref = port.argmax(want)
+    agree = [tok == ref]
+    for _ in range(8):
+        tok = eng.eval(np.array([ref], np.int32), lg)
+        want = pm.eval(np.array([ref], np.int32), threads=threads)[0]
+        ref = port.argmax(want)
+        agree.append(tok == ref)
+    assert all(agree), agree
+    eng.close()
