@@ -2,19 +2,22 @@
 // C[M][N] = X[M][K] . W[N][K]^T with the STORE / RESIDUAL / SWIGLU epilogues of the
 // FFMA GEMM (gemm_ffma.cu), for B200_PREC_TF32.
 //
-// One CTA computes one 128 x 128 tile of C (split over K when the tile grid
-// leaves SMs idle). Both operands are K-major in HBM (X rows are tokens, W rows
-// are output features), which is the layout tcgen05 reads directly:
+// A persistent grid (one CTA per SM) walks the 128 x 256 tiles of C (and the K
+// splits, when the tile grid alone leaves SMs idle). Both operands are K-major in
+// HBM (X rows are tokens, W rows are output features), the layout tcgen05 reads
+// directly:
 //   * warp 0, one lane: TMA engine. 2-D tiled copies (cuTensorMapEncodeTiled,
-//     128-byte swizzle) of a [128 rows x 32 floats] box of X and of W per stage
-//     into a kTStages-deep shared-memory ring, completing on the stage's mbarrier;
-//   * warp 1, one lane: tensor cores. Per stage four tcgen05.mma (M 128, N 128,
-//     K 8 each) from shared-memory descriptors into a 128-column F32
-//     accumulator in tensor memory; tcgen05.commit hands the stage back to the
-//     copy engine once the MMAs that read it are done, and a final commit
-//     signals the epilogue;
-//   * all four warps: epilogue. Warp w reads TMEM lanes 32w..32w+31 (= tile rows)
-//     with tcgen05.ld, 16 columns at a time, and writes C (or split-K partials).
+//     128-byte swizzle) of a [128 x 32 floats] box of X and a [256 x 32 floats] box
+//     of W per stage into a kTStages-deep shared-memory ring, completing on the
+//     stage's mbarrier;
+//   * warp 1, one lane: tensor cores. Per stage four tcgen05.mma (M 128, N 256,
+//     K 8 each) from shared-memory descriptors into one of two 256-column F32
+//     accumulators in tensor memory (the whole 512 columns of the SM);
+//     tcgen05.commit hands the stage back to the copy engine once the MMAs that
+//     read it are done, and signals the epilogue when a tile is complete;
+//   * warps 2..5: epilogue. Warp w reads TMEM lanes 32(w % 4)..+31 (= tile rows)
+//     with tcgen05.ld, 16 columns at a time, writes C (or split-K partials) and
+//     frees the accumulator, while the tensor cores already fill the other one.
 // TF32 multiplies use the top 19 bits of each F32 operand and accumulate in F32,
 // so results differ from the exact F32 reference by ~1e-3 relative (the
 // B200_PREC_TF32 tolerance); B200_PREC_FFMA is the exact path.
@@ -32,22 +35,27 @@
 namespace b200 {
 namespace {
 
-constexpr int kTBM = 128, kTBN = 128, kTBK = 32;  // kTBK floats = one 128-byte swizzle row
-constexpr int kTStages = 5;
-constexpr uint32_t kTileBytes = kTBM * kTBK * 4;  // 16 KB per operand per stage (kTBM == kTBN)
-constexpr uint32_t kStageBytes = 2 * kTileBytes;
-constexpr int kTThreads = 128;
-constexpr uint32_t kTmemCols = 128;  // F32 accumulator: 128 lanes x kTBN columns
-static_assert(kTBM == kTBN, "one box shape for both operands");
-static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocations are powers of two >= 32");
+constexpr int kTBM = 128, kTBK = 32;  // kTBK floats = one 128-byte swizzle row
+constexpr uint32_t kTileA = kTBM * kTBK * 4;  // 16 KB of X per stage
+constexpr int kEpiWarps = 4;                   // warps 2..5: TMEM lane quarters (warp % 4) 2, 3, 0, 1
+constexpr int kTThreads = 32 * (2 + kEpiWarps);
 
-constexpr size_t kTSmem = 1024 /* alignment slack */ + static_cast<size_t>(kTStages) * kStageBytes + 256;
-
-// Instruction descriptor of kind::tf32: F32 accumulate (bits 4-5 = 1), A and B TF32
-// (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22,
-// M >> 4 at bits 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kTBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kTBM >> 4) << 24);
+// Tile width BN (output features per tile): 256 when the tiles fill the SMs, else 128.
+template <int BN>
+struct TCfg {
+    static_assert(BN == 128 || BN == 256, "cta_group::1 MMA with M 128 takes N % 16 == 0, N <= 256");
+    static constexpr uint32_t kTileB = BN * kTBK * 4;  // W rows per stage
+    static constexpr uint32_t kStageBytes = kTileA + kTileB;
+    static constexpr int kStages = BN == 256 ? 4 : 6;  // 192 KB of ring either way: one CTA per SM
+    static constexpr uint32_t kAccCols = BN;            // one F32 accumulator: 128 lanes x BN columns
+    static constexpr uint32_t kTmemCols = 2 * BN;       // two, so a tile's epilogue overlaps the next tile's MMAs
+    static constexpr size_t kSmem = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes + 256;
+    // Instruction descriptor of kind::tf32: F32 accumulate (bits 4-5 = 1), A and B
+    // TF32 (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bits
+    // 17-22, M >> 4 at bits 24-28.
+    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                       (static_cast<uint32_t>(kTBM >> 4) << 24);
+};
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with the
 // 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte
@@ -74,11 +82,11 @@ B200_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, in
 B200_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 B200_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-B200_DEVICE void tc_mma_tf32(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+B200_DEVICE void tc_mma_tf32(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem),
-        "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
         : "memory");
 }
 
@@ -121,31 +129,52 @@ B200_DEVICE bool wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
 
 __device__ int32_t g_tf32_status;  // status word when the caller passes none
 
-template <int EPI>
+// Tile t of the persistent schedule: split z, then row block, then column block
+// (consecutive CTAs share a column block of W while X stays in L2).
+struct TileIx {
+    int64_t m0, n0, kbeg, kend;
+};
+template <int BN>
+B200_DEVICE TileIx tile_of(const GemmArgs &a, int64_t t, int64_t mt, int64_t nt) {
+    const int64_t z = t / (mt * nt), r = t % (mt * nt);
+    TileIx ix;
+    ix.m0 = (r % mt) * kTBM;
+    ix.n0 = (r / mt) * BN;
+    ix.kbeg = a.k_split ? z * a.k_split : 0;
+    ix.kend = a.k_split ? min64(a.K, ix.kbeg + a.k_split) : a.K;
+    return ix;
+}
+
+template <int EPI, int BN>
 __global__ void __launch_bounds__(kTThreads, 1)
-    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const GemmArgs a) {
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const GemmArgs a,
+                     int64_t n_tiles) {
+    using C = TCfg<BN>;
+    constexpr int kTStages = C::kStages;
+    constexpr uint32_t kStageBytes = C::kStageBytes, kAccCols = C::kAccCols, kTmemCols = C::kTmemCols;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t sbase = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
     unsigned char *gbase = smem_raw + (sbase - raw);
     uint64_t *full = reinterpret_cast<uint64_t *>(gbase + kTStages * kStageBytes);
     uint64_t *empty = full + kTStages;
-    uint64_t *done = empty + kTStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    uint64_t *acc_full = empty + kTStages;  // [2] accumulator b complete (tcgen05.commit)
+    uint64_t *acc_free = acc_full + 2;      // [2] accumulator b read out by the epilogue warps
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_free + 2);
     int32_t *status = a.status ? a.status : &g_tf32_status;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTBM, n0 = static_cast<int64_t>(blockIdx.x) * kTBN;
-    const int64_t kbeg = a.k_split ? static_cast<int64_t>(blockIdx.z) * a.k_split : 0;
-    const int64_t kend = a.k_split ? min64(a.K, kbeg + a.k_split) : a.K;
-    const int nk = static_cast<int>((kend - kbeg + kTBK - 1) / kTBK);
+    const int64_t mt = (a.M + kTBM - 1) / kTBM, nt = (a.N + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_free[b], kEpiWarps);
+        }
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmx)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
@@ -164,78 +193,142 @@ __global__ void __launch_bounds__(kTThreads, 1)
     grid_launch_dependents();
     grid_wait();  // X (and the residual) come from the previous kernel
 
-    if (warp == 0 && lane == 0) {
-        // ---- copy engine: stage s of k-step kt, after the MMAs of k-step kt - kTStages released it
-        int issued = 0;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- copy engine: ring stage it % kTStages over all k-steps of all tiles
+            int it = 0;
+            bool ok = true;
 #pragma unroll 1
-        for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % kTStages;
-            if (kt >= kTStages && !wait_bounded(&empty[s], ((kt / kTStages) - 1) & 1, status)) break;
-            const uint32_t dst = sbase + s * kStageBytes;
-            const int32_t kx = static_cast<int32_t>(kbeg + static_cast<int64_t>(kt) * kTBK);
-            mbar_arrive_expect_tx(&full[s], kStageBytes);
-            tma_load_2d(dst, &tmx, kx, static_cast<int32_t>(m0), smem_addr(&full[s]));
-            tma_load_2d(dst + kTileBytes, &tmw, kx, static_cast<int32_t>(n0), smem_addr(&full[s]));
-            ++issued;
-        }
-        // copies still landing in this CTA's shared memory: the last kTStages issued
+            for (int64_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const TileIx ix = tile_of<BN>(a, t, mt, nt);
 #pragma unroll 1
-        for (int kt = issued > kTStages ? issued - kTStages : 0; kt < issued; ++kt)
-            wait_bounded(&full[kt % kTStages], (kt / kTStages) & 1, nullptr);
-    } else if (warp == 1 && lane == 0) {
-        // ---- tensor cores
-#pragma unroll 1
-        for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % kTStages;
-            if (!wait_bounded(&full[s], (kt / kTStages) & 1, status)) break;
-            tc_fence_after();
-            const uint64_t da = desc_k_sw128(sbase + s * kStageBytes);
-            const uint64_t db = desc_k_sw128(sbase + s * kStageBytes + kTileBytes);
-#pragma unroll
-            for (int kk = 0; kk < kTBK / 8; ++kk)  // K 8 per MMA: +32 bytes = +2 in the address field
-                tc_mma_tf32(tmem, da + 2 * kk, db + 2 * kk, (kt | kk) != 0);
-            tc_commit(smem_addr(&empty[s]));
-        }
-        tc_commit(smem_addr(done));  // the accumulator is complete (or nothing was issued)
-    }
-    __syncwarp();
-
-    // ---- epilogue: thread (warp w, lane t) owns tile row 32w + t
-    // warp-uniform: tcgen05.ld below is a warp-collective (.sync.aligned) instruction
-    const bool have = __all_sync(0xffffffffu, wait_bounded(done, 0, status)) && nk > 0;
-    tc_fence_after();
-    if (have) {
-        const int64_t gm = m0 + 32 * warp + lane;
-        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-#pragma unroll 1
-        for (int c0 = 0; c0 < kTBN; c0 += 16) {
-            float v[16];
-            __syncwarp();
-            tc_ld16(trow + c0, v);  // warp-collective: every lane takes part
-            const int64_t gn = n0 + c0;
-            if (gm >= a.M || gn >= a.N) continue;
-            if (a.k_split) {  // raw partial sums of this split: ws[z][M][N]
-                float *ws = a.ws + static_cast<int64_t>(blockIdx.z) * a.M * a.N + gm * a.N;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (gn + j < a.N) ws[gn + j] = v[j];
-            } else if (EPI == GEMM_SWIGLU) {  // (gate, up) column pairs -> one output
-#pragma unroll
-                for (int j = 0; j < 16; j += 2)
-                    if (gn + j + 1 < a.N) {
-                        const float g = v[j], u = v[j + 1];
-                        const float sg = g / (1.0f + expf(-g));
-                        a.c[gm * a.ldc + (gn + j) / 2] = u * sg;
+                for (int64_t k = ix.kbeg; k < ix.kend; k += kTBK, ++it) {
+                    const int s = it % kTStages;
+                    if (it >= kTStages && !wait_bounded(&empty[s], ((it / kTStages) - 1) & 1, status)) {
+                        ok = false;
+                        break;
                     }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (gn + j < a.N) {
-                        float o = v[j];
-                        if (EPI == GEMM_RESIDUAL) o = o + a.r[gm * a.ldc + gn + j];
-                        a.c[gm * a.ldc + gn + j] = o;
-                    }
+                    const uint32_t dst = sbase + s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(dst, &tmx, static_cast<int32_t>(k), static_cast<int32_t>(ix.m0), smem_addr(&full[s]));
+                    tma_load_2d(dst + kTileA, &tmw, static_cast<int32_t>(k), static_cast<int32_t>(ix.n0),
+                                smem_addr(&full[s]));
+                }
             }
+            // copies still landing in this CTA's shared memory: the last kTStages issued
+#pragma unroll 1
+            for (int j = it > kTStages ? it - kTStages : 0; j < it; ++j)
+                wait_bounded(&full[j % kTStages], (j / kTStages) & 1, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- tensor cores: tile j of this CTA accumulates into TMEM columns (j % 2) * kAccCols
+            int it = 0, j = 0;
+            bool ok = true;
+#pragma unroll 1
+            for (int64_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++j) {
+                const TileIx ix = tile_of<BN>(a, t, mt, nt);
+                const int b = j & 1;
+                if (j >= 2 && !wait_bounded(&acc_free[b], ((j >> 1) - 1) & 1, status)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * kAccCols;
+                bool first = true;
+#pragma unroll 1
+                for (int64_t k = ix.kbeg; k < ix.kend; k += kTBK, ++it) {
+                    const int s = it % kTStages;
+                    if (!wait_bounded(&full[s], (it / kTStages) & 1, status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da = desc_k_sw128(sbase + s * kStageBytes);
+                    const uint64_t db = desc_k_sw128(sbase + s * kStageBytes + kTileA);
+#pragma unroll
+                    for (int kk = 0; kk < kTBK / 8; ++kk) {  // K 8 per MMA: +32 bytes = +2 in the address field
+                        tc_mma_tf32(acc, da + 2 * kk, db + 2 * kk, C::kIdesc, first ? 0u : 1u);
+                        first = false;
+                    }
+                    tc_commit(smem_addr(&empty[s]));
+                }
+                tc_commit(smem_addr(&acc_full[b]));  // this tile's accumulator is complete
+            }
+            // no MMA may still write tensor memory when it is freed (matters only if
+            // the epilogue gave up early)
+            if (j > 0) wait_bounded(&acc_full[(j - 1) & 1], ((j - 1) >> 1) & 1, nullptr);
+        }
+    } else {
+        // ---- epilogue warps: thread (warp w, lane t) owns tile row 32 * (w % 4) + t
+        const int q = warp & 3;
+        // 16-byte stores where C (and the split-K workspace) rows allow them
+        const bool vec_c = !(a.ldc & 3) && !(reinterpret_cast<uintptr_t>(a.c) & 15);
+        const bool vec_ws = !(a.N & 3) && !(reinterpret_cast<uintptr_t>(a.ws) & 15);
+        int j = 0;
+#pragma unroll 1
+        for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++j) {
+            const TileIx ix = tile_of<BN>(a, t, mt, nt);
+            const int b = j & 1;
+            // warp-uniform: tcgen05.ld is a warp-collective (.sync.aligned) instruction
+            if (!__all_sync(0xffffffffu, wait_bounded(&acc_full[b], (j >> 1) & 1, status))) break;
+            tc_fence_after();
+            const int64_t gm = ix.m0 + 32 * q + lane;
+            const uint32_t trow = tmem + b * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
+            const int64_t z = t / (mt * nt);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                __syncwarp();
+                tc_ld16(trow + c0, v);  // every lane takes part
+                const int64_t gn = ix.n0 + c0;
+                if (gm >= a.M || gn >= a.N) continue;
+                const bool whole = gn + 16 <= a.N;
+                if (a.k_split) {  // raw partial sums of this split: ws[z][M][N]
+                    float *ws = a.ws + z * a.M * a.N + gm * a.N + gn;
+                    if (whole && vec_ws) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4 *>(ws + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (gn + i < a.N) ws[i] = v[i];
+                    }
+                } else if (EPI == GEMM_SWIGLU) {  // (gate, up) column pairs -> one output
+                    float h[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float g = v[2 * i], u = v[2 * i + 1];
+                        const float sg = g / (1.0f + expf(-g));
+                        h[i] = u * sg;
+                    }
+                    float *dst = a.c + gm * a.ldc + gn / 2;
+                    if (whole && vec_c) {
+                        *reinterpret_cast<float4 *>(dst) = make_float4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<float4 *>(dst + 4) = make_float4(h[4], h[5], h[6], h[7]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            if (gn + 2 * i + 1 < a.N) dst[i] = h[i];
+                    }
+                } else {
+                    float *dst = a.c + gm * a.ldc + gn;
+                    if (EPI == GEMM_RESIDUAL) {
+                        const float *res = a.r + gm * a.ldc + gn;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (gn + i < a.N) v[i] = v[i] + res[i];
+                    }
+                    if (whole && vec_c) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (gn + i < a.N) dst[i] = v[i];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_free[b]);  // the MMA warp may reuse accumulator b
         }
     }
     tc_fence_before();
@@ -264,68 +357,81 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// [rows][cols] F32 matrix with row stride `ld` floats, boxes of [128 rows x 32 floats].
-bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld) {
+// [rows][cols] F32 matrix with row stride `ld` floats, boxes of [box_rows x 32 floats].
+bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-    const cuuint32_t box[2] = {kTBK, kTBM};
+    const cuuint32_t box[2] = {kTBK, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI>
-cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a, dim3 grid, cudaStream_t st,
-                       bool pdl) {
+template <int EPI, int BN>
+cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a, int64_t n_tiles,
+                       cudaStream_t st, bool pdl) {
     static bool attr_set = false;
     if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kTSmem));
+        const cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<EPI, BN>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(TCfg<BN>::kSmem));
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    return b200_launch(gemm_tf32_kernel<EPI>, grid, dim3(kTThreads), kTSmem, st, pdl, mx, mw, a);
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_tiles, device_sm_count())));
+    return b200_launch(gemm_tf32_kernel<EPI, BN>, grid, dim3(kTThreads), TCfg<BN>::kSmem, st, pdl, mx, mw, a, n_tiles);
+}
+
+template <int BN>
+cudaError_t launch_bn(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
+    GemmArgs a = a_in;
+    CUtensorMap mx, mw;
+    if (!encode(&mx, a.x, a.M, a.K, a.ldx, kTBM) || !encode(&mw, a.w, a.N, a.K, a.K, BN)) return cudaErrorNotSupported;
+    const int64_t tiles = ((a.N + BN - 1) / BN) * ((a.M + kTBM - 1) / kTBM);
+    // Split K when the tile grid leaves SMs idle (short prompts): about one tile per
+    // SM, at least 256 of K per split, partials reduced in split order.
+    a.k_split = 0;
+    int64_t splits = 1;
+    const int64_t target = device_sm_count();
+    if (a.ws && tiles < target && a.K >= 512) {
+        splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
+        while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
+        if (splits > 1) {
+            a.k_split = ((a.K + splits - 1) / splits + kTBK - 1) / kTBK * kTBK;
+            splits = (a.K + a.k_split - 1) / a.k_split;
+        } else {
+            splits = 1;
+        }
+    }
+    const int64_t n_tiles = tiles * splits;
+    if (a.k_split) {
+        const cudaError_t e = launch_epi<GEMM_STORE, BN>(mx, mw, a, n_tiles, stream, pdl);
+        if (e != cudaSuccess) return e;
+        return gemm_splitk_reduce_launch(a, static_cast<int>(splits), stream, pdl);
+    }
+    switch (a.epi) {
+        case GEMM_STORE: return launch_epi<GEMM_STORE, BN>(mx, mw, a, n_tiles, stream, pdl);
+        case GEMM_RESIDUAL: return launch_epi<GEMM_RESIDUAL, BN>(mx, mw, a, n_tiles, stream, pdl);
+        case GEMM_SWIGLU: return launch_epi<GEMM_SWIGLU, BN>(mx, mw, a, n_tiles, stream, pdl);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-cudaError_t gemm_tf32_launch(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
-    GemmArgs a = a_in;
+cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;
     if (a.epi == GEMM_SWIGLU && (a.N & 1)) return cudaErrorInvalidValue;
     // TMA: 16-byte aligned bases and row strides; the tile rows must fit 32-bit coordinates
     if ((a.K & 3) || (a.ldx & 3) || (reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
         a.M >= (int64_t(1) << 31) || a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 31))
         return cudaErrorNotSupported;
-    CUtensorMap mx, mw;
-    if (!encode(&mx, a.x, a.M, a.K, a.ldx) || !encode(&mw, a.w, a.N, a.K, a.K)) return cudaErrorNotSupported;
-    dim3 grid(static_cast<unsigned>((a.N + kTBN - 1) / kTBN), static_cast<unsigned>((a.M + kTBM - 1) / kTBM));
-    // Split K when the tile grid leaves SMs idle (short prompts): about one CTA per
-    // SM, at least 256 of K per split, partials reduced in split order.
-    a.k_split = 0;
-    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y, target = device_sm_count();
-    if (a.ws && tiles < target && a.K >= 512) {
-        int64_t splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
-        while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
-        if (splits > 1) {
-            a.k_split = ((a.K + splits - 1) / splits + kTBK - 1) / kTBK * kTBK;
-            grid.z = static_cast<unsigned>((a.K + a.k_split - 1) / a.k_split);
-        }
-    }
-    if (a.k_split) {
-        const cudaError_t e = launch_epi<GEMM_STORE>(mx, mw, a, grid, stream, pdl);
-        if (e != cudaSuccess) return e;
-        return gemm_splitk_reduce_launch(a, static_cast<int>(grid.z), stream, pdl);
-    }
-    switch (a.epi) {
-        case GEMM_STORE: return launch_epi<GEMM_STORE>(mx, mw, a, grid, stream, pdl);
-        case GEMM_RESIDUAL: return launch_epi<GEMM_RESIDUAL>(mx, mw, a, grid, stream, pdl);
-        case GEMM_SWIGLU: return launch_epi<GEMM_SWIGLU>(mx, mw, a, grid, stream, pdl);
-    }
-    return cudaErrorInvalidValue;
+    // 256-wide tiles (half the X traffic per flop) once they alone fill the SMs
+    const int64_t tiles256 = ((a.N + 255) / 256) * ((a.M + kTBM - 1) / kTBM);
+    return tiles256 >= device_sm_count() ? launch_bn<256>(a, stream, pdl) : launch_bn<128>(a, stream, pdl);
 }
 
 }  // namespace b200
