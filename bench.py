@@ -123,8 +123,8 @@ def model_cfg(name):
     return {"0.6b": G.QWEN3_0_6B, "8b": G.QWEN3_8B}[name]
 
 
-def prompt_ids(cfg):
-    return np.random.default_rng(SEED).integers(0, cfg.n_vocab, PROMPT_LEN).astype(np.int32)
+def prompt_ids(cfg, n=PROMPT_LEN):
+    return np.random.default_rng(SEED).integers(0, cfg.n_vocab, n).astype(np.int32)
 
 
 def step_bytes(cfg, ctx_len: int) -> int:
@@ -212,10 +212,10 @@ def run_b200(args):
         dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
     cfg = model_cfg(args.model)
     tp = args.model == "8b" and world > 1
-    steps, warm = args.steps, args.warmup
-    cap = PROMPT_LEN + max(steps, 128) + warm + 8
+    steps, warm, plen = args.steps, args.warmup, args.prompt
+    cap = plen + max(steps, 128) + warm + 8
     mode = {"auto": B.DECODE_AUTO, "multi": B.DECODE_MULTI, "single": B.DECODE_SINGLE}[args.decode]
-    eng = B.Engine(cfg, kv_capacity=cap, max_batch=PROMPT_LEN, device=local,
+    eng = B.Engine(cfg, kv_capacity=cap, max_batch=plen, device=local,
                    tp_rank=rank if tp else 0, tp_world=world if tp else 1, decode_mode=mode)
     if args.model == "0.6b":
         if world > 1 and local != 0:
@@ -231,7 +231,7 @@ def run_b200(args):
         dist.broadcast_object_list(uid, src=0)
         eng.tp_init(uid[0])
     eng.finalize()
-    prompt = prompt_ids(cfg)
+    prompt = prompt_ids(cfg, plen)
     stream = torch.cuda.ExternalStream(eng.stream())
 
     def barrier():
@@ -243,14 +243,21 @@ def run_b200(args):
     eng.reset()
     eng.eval(prompt)
     eng.generate(warm)
-    # ---- TTFT: prefill of the 32-token prompt + first greedy token (host ids in, token out)
-    ttft = []
-    for _ in range(3):
-        eng.reset()
-        barrier()
-        t0 = time.perf_counter()
-        first = eng.eval(prompt)
-        ttft.append((time.perf_counter() - t0) * 1e3)
+    # ---- TTFT: prefill of the prompt + first greedy token (host ids in, token out), with
+    # the exact F32 FFMA prefill GEMMs and, beside it, with the TF32 tensor-core ones
+    def time_prefill():
+        out = []
+        for _ in range(3):
+            eng.reset()
+            barrier()
+            t0 = time.perf_counter()
+            tok = eng.eval(prompt)
+            out.append((time.perf_counter() - t0) * 1e3)
+        return out, tok
+    eng.set_precision(B.PREC_TF32)
+    ttft_tf32, first_tf32 = time_prefill()
+    eng.set_precision(B.PREC_FFMA)
+    ttft, first = time_prefill()
     # ---- value: K decode steps, device resident, CUDA events on the engine stream
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -296,19 +303,22 @@ def run_b200(args):
         trace = trace_summary_mk(eng.trace(), cfg, clk.summary().get("sm_mhz") or 1965.0) if launches == 1 \
             else trace_summary(eng.trace(), cfg)
     hbm, peak_kind = peaks()
-    ctx_mid = PROMPT_LEN + steps // 2
+    ctx_mid = plen + steps // 2
     res = {
-        "metric": METRIC if args.model == "0.6b" else METRIC.replace("0.6B", "8B") + f" TP{world}",
+        "metric": (METRIC if args.model == "0.6b" else METRIC.replace("0.6B", "8B") + f" TP{world}").replace(
+            "32-token", f"{plen}-token"),
         "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"Qwen3-{'0.6B' if args.model == '0.6b' else '8B'} F32 decode, bs1, prompt "
-                               f"{PROMPT_LEN}, positions {PROMPT_LEN}..{PROMPT_LEN + steps - 1}",
+                               f"{plen}, positions {plen}..{plen + steps - 1}",
                    "weights": f"seeded N(0,0.02) ({'GGUF' if args.model == '0.6b' else 'on-device Philox'}, seed {SEED})",
                    "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
                    "l2": f"inputs larger than L2 ({cfg.weight_bytes_per_token / 1e9:.2f} GB of weights "
                          f"streamed per step{' over all ranks' if tp else ''})"},
         "ttft_ms": round(float(np.median(ttft)), 3),
+        "ttft_ms_tf32": round(float(np.median(ttft_tf32)), 3),
+        "first_token_tf32_equal": bool(first_tf32 == first),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": steps * launches * world,  # every rank launches its own
         "clocks": clk.summary(),
@@ -392,14 +402,14 @@ def run_reference(args):
     threads = args.cpu_threads or (os.cpu_count() or 1)
     ref = oracle.Ref()
     path = G.cached_model(cfg, SEED)
-    steps, warm = args.steps, args.warmup
-    eng = oracle.RefEngine(ref, path, threads=threads, capacity=PROMPT_LEN + steps + warm + 8)
-    tok = eng.eval(prompt_ids(cfg))
+    steps, warm, plen = args.steps, args.warmup, args.prompt
+    eng = oracle.RefEngine(ref, path, threads=threads, capacity=plen + steps + warm + 8)
+    tok = eng.eval(prompt_ids(cfg, plen))
     for _ in range(warm):
         tok = eng.eval(np.array([tok], np.int32))
     eng.reset()
     t0 = time.perf_counter()
-    tok = eng.eval(prompt_ids(cfg))
+    tok = eng.eval(prompt_ids(cfg, plen))
     ttft = time.perf_counter() - t0
     t1 = time.perf_counter()
     for _ in range(steps):
@@ -408,15 +418,15 @@ def run_reference(args):
     eng.close()
     value = steps / dt
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC.replace("32-token", f"{plen}-token"), "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"Qwen3-0.6B F32 decode, bs1, prompt {PROMPT_LEN}, positions "
-                               f"{PROMPT_LEN}..{PROMPT_LEN + steps - 1}", "weights": f"seeded GGUF seed {SEED}",
+        "config": {"workload": f"Qwen3-0.6B F32 decode, bs1, prompt {plen}, positions "
+                               f"{plen}..{plen + steps - 1}", "weights": f"seeded GGUF seed {SEED}",
                    "parallelism": "single"},
         "ttft_ms": round(ttft * 1e3, 1),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{steps} greedy decode tokens after a {PROMPT_LEN}-token prefill"},
+                         "sample": f"{steps} greedy decode tokens after a {plen}-token prefill"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -490,6 +500,8 @@ def main():
     ap.add_argument("--precision", type=int, default=0)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN,
+                    help="prompt tokens before the timed decode (BASELINE configs: 32, 256, 2048)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--model", choices=["0.6b", "8b"], default="0.6b")

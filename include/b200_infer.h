@@ -213,6 +213,10 @@ int b200_engine_finalize(b200_engine *e);
 
 /* Drops the sequence (n_past = 0). */
 int b200_engine_reset(b200_engine *e);
+/* Precision of the prefill matrix products from the next step on (B200_PREC_FFMA:
+ * exact F32; B200_PREC_TF32: tcgen05 tensor cores). Decode is unaffected (its
+ * matrix-vector products are F32 FFMA either way). */
+int b200_engine_set_precision(b200_engine *e, int32_t precision);
 int64_t b200_engine_n_past(const b200_engine *e);
 
 /* Kernel launches of this library per decode step after finalize: 1 when the

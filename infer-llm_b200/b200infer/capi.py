@@ -66,6 +66,7 @@ _SIGS = {
     "b200_engine_finalize": ([_vp], C.c_int),
     "b200_engine_reset": ([_vp], C.c_int),
     "b200_engine_n_past": ([_vp], _i64),
+    "b200_engine_set_precision": ([_vp, C.c_int32], C.c_int),
     "b200_engine_decode_launches": ([_vp], C.c_int),
     "b200_engine_eval": ([_vp, _vp, _i64, _vp, _vp], C.c_int),
     "b200_engine_generate": ([_vp, _i64, _vp], C.c_int),

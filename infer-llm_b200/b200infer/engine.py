@@ -92,6 +92,10 @@ class Engine:
     def reset(self):
         _chk("b200_engine_reset", lib().b200_engine_reset(self.h))
 
+    def set_precision(self, precision: int):
+        """Prefill matrix-product precision from the next step on (PREC_FFMA / PREC_TF32)."""
+        _chk("b200_engine_set_precision", lib().b200_engine_set_precision(self.h, precision))
+
     @property
     def n_past(self) -> int:
         return int(lib().b200_engine_n_past(self.h))

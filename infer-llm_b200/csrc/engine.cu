@@ -126,7 +126,8 @@ struct b200_engine {
     cudaGraphExec_t graph_exec = nullptr;
     bool graph_logits = false;
     b200_tp *tp = nullptr;
-    int32_t *pinned_io = nullptr;  // small pinned host buffer for per-step ids / tokens
+    int32_t *pinned_io = nullptr;  // pinned host buffer: [max_batch] step ids, then the sampled token
+    int64_t io_tok = 0;            // index of the token slot in pinned_io (past the ids, 64-byte aligned)
     // device-side step trace (b200_engine_trace_step): 8 x u64 per launch
     unsigned long long *trace_buf = nullptr;
     int trace_cap = 0, trace_n = 0;
@@ -659,7 +660,8 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     if (err == cudaSuccess) err = cudaMalloc(&e->w_arena, e->w_bytes);
     if (err == cudaSuccess) err = cudaMalloc(&e->kv_arena, e->kv_bytes);
     if (err == cudaSuccess) err = cudaMalloc(&e->act_arena, e->act_bytes);
-    if (err == cudaSuccess) err = cudaMallocHost(&e->pinned_io, 4096);
+    e->io_tok = (static_cast<int64_t>(c.max_batch) + 15) / 16 * 16;
+    if (err == cudaSuccess) err = cudaMallocHost(&e->pinned_io, static_cast<size_t>(e->io_tok + 16) * 4);
     if (err != cudaSuccess) {
         b200_engine_destroy(e);
         cudaGetLastError();
@@ -930,6 +932,12 @@ int b200_engine_reset(b200_engine *e) {
 
 int64_t b200_engine_n_past(const b200_engine *e) { return e ? e->n_past : -1; }
 
+int b200_engine_set_precision(b200_engine *e, int32_t precision) {
+    if (!e || (precision != B200_PREC_FFMA && precision != B200_PREC_TF32)) return B200_ERR_INVALID_ARGUMENT;
+    e->c.precision = precision;
+    return B200_OK;
+}
+
 int b200_engine_decode_launches(const b200_engine *e) {
     if (!e || !e->finalized) return -B200_ERR_INVALID_ARGUMENT;
     if (e->use_mk) return 1;
@@ -964,7 +972,7 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
             rc = enqueue_prefill(e, static_cast<int>(n), want_logits);
         if (rc != B200_OK) return rc;
     }
-    B200_TRY(cudaMemcpyAsync(e->pinned_io + 1024, e->token, 4, cudaMemcpyDeviceToHost, st));
+    B200_TRY(cudaMemcpyAsync(e->pinned_io + e->io_tok, e->token, 4, cudaMemcpyDeviceToHost, st));
     if (want_logits && e->c.tp_world == 1)
         B200_TRY(cudaMemcpyAsync(host_last_logits, e->logits, static_cast<size_t>(e->V) * 4, cudaMemcpyDeviceToHost, st));
     rc = check_status(e);  // synchronizes
@@ -974,7 +982,7 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
         cudaMemcpy(e->n_past_dev, &np, 4, cudaMemcpyHostToDevice);
         return rc;
     }
-    if (host_token) *host_token = e->pinned_io[1024];
+    if (host_token) *host_token = e->pinned_io[e->io_tok];
     e->n_past += n;
     return B200_OK;
 }

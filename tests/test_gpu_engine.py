@@ -164,3 +164,27 @@ def test_qwen3_06b_teacher_forced(cuda, port, steps, mode):
     assert all(agree), agree
     assert worst <= 1e-4, worst
     eng.close()
+
+
+def test_prompt_longer_than_1024(cuda, port, tmp_path):
+    """A 1,500-token prefill (host ids staged through the engine's pinned buffer,
+    which holds max_batch ids plus the sampled-token slot) agrees with the
+    restatement, and decode continues from it."""
+    cfg = G.Qwen3Config(n_vocab=1000, n_embd=256, n_layer=2, n_head=4, n_head_kv=2, head_dim=64, n_ff=512,
+                        n_ctx_train=4096)
+    path = str(tmp_path / "m.gguf")
+    G.write_gguf(path, cfg, seed=9)
+    rd = G.GGUFReader(path)
+    pm = oracle.PortQwen3(port, cfg.as_dict(), {n: np.array(rd.tensor(n)) for n in rd.names()}, kv_capacity=1600)
+    eng = B.Engine(cfg, kv_capacity=1600, max_batch=1500).load_gguf(path).finalize()
+    prompt = np.random.default_rng(5).integers(0, cfg.n_vocab, 1500).astype(np.int32)
+    lg = np.empty(cfg.n_vocab, np.float32)
+    tok = eng.eval(prompt, lg)
+    want = pm.eval(prompt, threads=THREADS)[0]
+    assert rel_err(lg, want) <= 1e-4 and tok == port.argmax(want)
+    for _ in range(3):
+        nxt = eng.eval(np.array([tok], np.int32), lg)
+        want = pm.eval(np.array([tok], np.int32), threads=THREADS)[0]
+        assert rel_err(lg, want) <= 1e-4 and nxt == port.argmax(want)
+        tok = nxt
+    eng.close()
