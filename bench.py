@@ -436,44 +436,70 @@ def run_op(args):
 
     --op gemv|gemm: y = x.W^T with W (N, K) ~ N(0, 0.02), x (M, K) ~ N(0, 1);
     --op attn: GQA attention (16 q / 8 kv heads, d 128), decode (--M 1, --L cache
-    length) or prefill (--M tokens, causal). Each launch is timed with CUDA events on
-    the launching stream; between launches a 256 MB buffer is overwritten so the
-    next launch starts with a cold L2. Prints one JSON line per shape.
+    length) or prefill (--M tokens, causal);
+    --op sweep: every shape of configs[1] (the six projection shapes of a layer plus
+    the LM head at M = 1, 32, 256; M > 4 with the FFMA and the TF32 GEMM) and
+    configs[2] (prefill S = 32..2048, decode L = 256..8192) in one process.
+    Each launch is timed with CUDA events on the launching stream; between launches
+    a 256 MB buffer is overwritten so the next launch starts with a cold L2. Prints
+    one JSON line per shape.
     """
     import torch
-    import b200infer as B
     torch.cuda.set_device(0)
+    if args.op == "sweep":
+        cases = []
+        for (K, N) in [(1024, 2048), (1024, 1024), (2048, 1024), (1024, 3072), (3072, 1024), (1024, 151936)]:
+            for M in (1, 32, 256):
+                if M <= 4:
+                    cases.append(dict(op="gemv", K=K, N=N, M=M, L=0, precision=0))
+                else:
+                    for prec in (0, 1):
+                        cases.append(dict(op="gemm", K=K, N=N, M=M, L=0, precision=prec))
+        for S in (32, 64, 128, 256, 2048):
+            cases.append(dict(op="attn", K=0, N=0, M=S, L=S, precision=0))
+        for L in (256, 1024, 4096, 8192):
+            cases.append(dict(op="attn", K=0, N=0, M=1, L=L, precision=0))
+    else:
+        cases = [dict(op=args.op, K=args.K, N=args.N, M=args.M, L=args.L, precision=args.precision)]
+    for c in cases:
+        print(json.dumps(op_case(c, args.steps, args.warmup)), flush=True)
+
+
+def op_case(c, steps, warmup):
+    import torch
+    import b200infer as B
     dev = torch.device("cuda:0")
     hbm, peak_kind = peaks()
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
     g = torch.Generator(device=dev).manual_seed(1)
     st = torch.cuda.current_stream()
-    res = {"op": args.op, "K": args.K, "N": args.N, "M": args.M, "L": args.L}
-    if args.op in ("gemv", "gemm"):
-        w = torch.randn((args.N, args.K), device=dev, generator=g) * 0.02
-        x = torch.randn((args.M, args.K), device=dev, generator=g)
-        out = torch.empty((args.M, args.N), device=dev)
-        fn = lambda: B.mul_mat(w, x, precision=args.precision, out=out)
-        nbytes = 4 * (args.N * args.K + args.M * args.K + args.M * args.N)
-        flops = 2 * args.M * args.N * args.K
+    res = dict(c)
+    if c["op"] in ("gemv", "gemm"):
+        K, N, M = c["K"], c["N"], c["M"]
+        w = torch.randn((N, K), device=dev, generator=g) * 0.02
+        x = torch.randn((M, K), device=dev, generator=g)
+        out = torch.empty((M, N), device=dev)
+        fn = lambda: B.mul_mat(w, x, precision=c["precision"], out=out)
+        nbytes = 4 * (N * K + M * K + M * N)
+        flops = 2 * M * N * K
     else:
         Hq, Hkv, D = 16, 8, 128
-        L = args.L if args.M == 1 else args.M
-        n_past = L - args.M
-        q = torch.randn((args.M, Hq, D), device=dev, generator=g)
+        M = c["M"]
+        L = c["L"] if M == 1 else M
+        n_past = L - M
+        q = torch.randn((M, Hq, D), device=dev, generator=g)
         k = torch.randn((L, Hkv, D), device=dev, generator=g)
         v = torch.randn((L, Hkv, D), device=dev, generator=g)
         out = torch.empty_like(q)
-        ws = torch.empty(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, args.M, L), dtype=torch.uint8,
-                         device=dev)
+        ws = torch.empty(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, M, L), dtype=torch.uint8, device=dev)
         fn = lambda: B.flash_attn(q, k, v, n_past, out=out, workspace=ws)
-        nbytes = 4 * (2 * L * Hkv * D + 2 * args.M * Hq * D)
-        causal_pairs = args.M * n_past + args.M * (args.M + 1) / 2
+        nbytes = 4 * (2 * L * Hkv * D + 2 * M * Hq * D)
+        causal_pairs = M * n_past + M * (M + 1) / 2
         flops = 4 * Hq * D * causal_pairs
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         fn()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
@@ -486,12 +512,12 @@ def run_op(args):
                 "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "tflops": round(flops / (us * 1e-6) / 1e12, 3),
                 "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4), "peak_kind": peak_kind,
                 "l2": "flushed between launches"})
-    print(json.dumps(res), flush=True)
+    return res
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["gemv", "gemm", "attn"], default=None,
+    ap.add_argument("--op", choices=["gemv", "gemm", "attn", "sweep"], default=None,
                     help="op-level timing instead of the end-to-end decode benchmark")
     ap.add_argument("--K", type=int, default=1024)
     ap.add_argument("--N", type=int, default=1024)
