@@ -441,8 +441,9 @@ def run_op(args):
     the LM head at M = 1, 32, 256; M > 4 with the FFMA and the TF32 GEMM) and
     configs[2] (prefill S = 32..2048, decode L = 256..8192) in one process.
     Each launch is timed with CUDA events on the launching stream; between launches
-    a 256 MB buffer is overwritten so the next launch starts with a cold L2. Prints
-    one JSON line per shape.
+    a 256 MB buffer is overwritten so the next launch starts with a cold L2, and a
+    device-side sleep covers the host's submission of the launch. Prints one JSON
+    line per shape.
     """
     import torch
     torch.cuda.set_device(0)
@@ -491,7 +492,7 @@ def op_case(c, steps, warmup):
         k = torch.randn((L, Hkv, D), device=dev, generator=g)
         v = torch.randn((L, Hkv, D), device=dev, generator=g)
         out = torch.empty_like(q)
-        ws = torch.empty(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, M, L), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, M, L), dtype=torch.uint8, device=dev)
         fn = lambda: B.flash_attn(q, k, v, n_past, out=out, workspace=ws)
         nbytes = 4 * (2 * L * Hkv * D + 2 * M * Hq * D)
         causal_pairs = M * n_past + M * (M + 1) / 2
@@ -501,6 +502,9 @@ def op_case(c, steps, warmup):
     times = []
     for _ in range(steps):
         flush.zero_()
+        # keep the GPU busy (~100 us) while the host submits the op, so the events time
+        # the kernel and not the Python call overhead in front of it
+        torch.cuda._sleep(200_000)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         fn()

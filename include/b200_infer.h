@@ -106,11 +106,16 @@ void b200_rope_freqs(float theta, int64_t D, float *host_freq);
  * k[t*k_tok_stride + h*k_head_stride + d] (the reference cache is token-major:
  * k_tok_stride = Hkv*D, k_head_stride = D); out [D, Hq, Tq].
  * Key j is visible to query i iff j <= n_past + i; Tkv = n_past + Tq.
- * scale <= 0 selects 1/sqrt(D). Decode (Tq == 1) uses split-KV flash-decoding whose
- * splits of one KV head form a thread-block cluster and merge through distributed
- * shared memory; Tq > 1 uses a tiled online-softmax kernel. Neither needs global
- * scratch today: `workspace` may be NULL (b200_flash_attn_workspace_bytes returns
- * the size a future variant would need, currently 0 for decode).
+ * scale <= 0 selects 1/sqrt(D). Decode (Tq == 1) uses split-KV flash-decoding over
+ * about 128 keys per CTA: with a workspace of b200_flash_attn_workspace_bytes(...)
+ * bytes the K/V rows are staged by bulk copies (TMA engine) into a shared-memory
+ * ring and the splits' partials are merged through the workspace by the last CTA
+ * of each KV head. The workspace must be zero-filled before its first use and may
+ * be reused by later calls (every completed call leaves it ready); after a call that
+ * reported a device error, zero it again. With `workspace` NULL (or smaller), at
+ * most 16 splits per KV head form a thread-block cluster and merge through
+ * distributed shared memory instead. Tq > 1 uses a tiled online-softmax kernel and
+ * needs no workspace.
  * Replaces CUDA_F32::compute_flash_attn (kernel_f32.hpp:24, kernel_f32.cu:452-511),
  * which mallocs an Hq*Tq*Tkv score matrix and synchronizes on every call. */
 int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D,

@@ -169,15 +169,19 @@ def qk_norm_rope(q, k, q_gamma, k_gamma, freq, pos, eps, n_ctx, v=None, k_out=No
 
 
 def flash_attn(q, k, v, n_past, scale=0.0, out=None, workspace=None):
-    """q (Tq, Hq, D); k, v (Tkv, Hkv, D) token-major; returns (Tq, Hq, D)."""
+    """q (Tq, Hq, D); k, v (Tkv, Hkv, D) token-major; returns (Tq, Hq, D).
+
+    workspace: a zero-filled uint8 tensor of b200_flash_attn_workspace_bytes bytes
+    (reusable across calls), or None for a fresh one; pass an empty tensor to run
+    decode without one (the cluster-merged path)."""
     import torch
     _dev_check(q, k, v)
     Tq, Hq, D = q.shape
     Tkv, Hkv, _ = k.shape
     out = out if out is not None else torch.empty_like(q)
     nbytes = lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, Tq, Tkv)
-    if workspace is None:
-        workspace = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
+    if workspace is None:  # zero-filled: the decode split counters start at zero
+        workspace = torch.zeros(nbytes, device=q.device, dtype=torch.uint8)
     _chk("b200_flash_attn", lib().b200_flash_attn(
         _p(q), _p(k), _p(v), _p(out), D, Hq, Hkv, Tq, Tkv, n_past, scale, Hkv * D, D, Hkv * D, D,
         _p(workspace), workspace.numel(), _stream()))

@@ -13,6 +13,7 @@ struct AttnArgs {
     int64_t k_tok = 0, k_head = 0, v_tok = 0, v_head = 0;
     int64_t D = 0, Hq = 0, Hkv = 0, Tq = 0;
     int64_t n_past = 0;                  // host value, used when n_past_dev is null
+    int64_t kv_rows = 0;                 // positions the K/V buffers hold (0: n_past + 1)
     const int32_t *n_past_dev = nullptr; // device scalar (graph-replayed decode)
     float scale = 0.f;
     void *ws = nullptr;                  // decode split partials + counters
@@ -38,9 +39,12 @@ struct AttnArgs {
 };
 
 // Decode (Tq == 1): fixed `splits` x Hkv CTAs, each a slice of [0, n_past+1),
-// merged in-kernel by the last CTA of each KV head. Counters in `ws` must be zero
-// before the first launch (the kernel re-zeroes them).
-int attn_decode_splits(int64_t max_len);
+// merged in-kernel by the last CTA of each KV head. With a workspace of at least
+// attn_decode_ws_bytes(...) the K/V tiles are staged by bulk copies and the split
+// partials merged through it; its counters (the last Hkv words) must be zero before
+// the first launch and every completed launch leaves them zero. Without one, at
+// most 16 splits form a thread-block cluster and merge in distributed shared memory.
+int attn_decode_splits(int64_t max_len, int64_t Hkv);
 size_t attn_decode_ws_bytes(int64_t D, int64_t Hq, int64_t Hkv, int splits);
 cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t stream, bool pdl);
 

@@ -144,7 +144,7 @@ int b200_qk_norm_rope(const float *q_in, int64_t q_ld, const float *k_in, int64_
 
 size_t b200_flash_attn_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tkv) {
     if (Tq != 1) return 256;
-    return attn_decode_ws_bytes(D, Hq, Hkv, attn_decode_splits(Tkv));
+    return attn_decode_ws_bytes(D, Hq, Hkv, attn_decode_splits(Tkv, Hkv));
 }
 
 int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D, int64_t Hq,
@@ -174,9 +174,10 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
     a.ws_bytes = workspace_bytes;
     cudaStream_t st = as_stream(stream);
     if (Tq == 1) {
-        // split-KV decode; the splits of a KV head merge through distributed shared
-        // memory inside one thread-block cluster, so no workspace is used
-        const int S = attn_decode_splits(Tkv);
+        // split-KV decode: with the workspace of b200_flash_attn_workspace_bytes the
+        // K/V tiles are bulk-copied and the splits merged through it; without one the
+        // splits of a KV head merge in distributed shared memory (one cluster)
+        const int S = attn_decode_splits(Tkv, Hkv);
         return from_cuda(attn_decode_launch(a, S, st, false));
     }
     return from_cuda(attn_prefill_launch(a, st, false));

@@ -273,6 +273,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         a.Hkv = e->Hkv;
         a.Tq = M;
         a.n_past_dev = e->n_past_dev;
+        a.kv_rows = e->c.kv_capacity;
         a.ws = e->attn_ws;
         a.ws_bytes = e->attn_ws_bytes;
         a.status = e->status;
@@ -527,8 +528,9 @@ int check_status(b200_engine *e) {
     B200_TRY(cudaStreamSynchronize(e->stream));
     if (s == 0) return B200_OK;
     B200_TRY(cudaMemsetAsync(e->status, 0, 4, e->stream));
-    // an aborted step may leave argmax tickets behind
+    // an aborted step may leave argmax tickets and attention split counters behind
     B200_TRY(cudaMemsetAsync(e->am_counter, 0, 4, e->stream));
+    if (e->attn_ws_bytes) B200_TRY(cudaMemsetAsync(e->attn_ws, 0, e->attn_ws_bytes, e->stream));
     B200_TRY(cudaStreamSynchronize(e->stream));
     if (s == B200_DEV_BAD_LOGITS) return B200_ERR_NUMERIC;
     if (s == B200_DEV_TIMEOUT) return B200_ERR_TIMEOUT;
@@ -625,7 +627,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t kv_layer = align_up(static_cast<size_t>(cap * e->Hkv * D) * 4, A) * 2;
     e->kv_bytes = kv_layer * NL;
     // ---- activation arena
-    e->attn_splits = attn_decode_splits(cap);
+    e->attn_splits = attn_decode_splits(cap, e->Hkv);
     e->attn_ws_bytes = attn_decode_ws_bytes(D, e->Hq, e->Hkv, e->attn_splits);
     off = 0;
     const size_t o_x = take(MB * H), o_xn = take(MB * H), o_qkv = take(MB * e->qkv_rows);

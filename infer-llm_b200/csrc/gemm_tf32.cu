@@ -25,12 +25,10 @@
 // Every mbarrier wait is bounded: a wait that runs out records B200_DEV_TIMEOUT in
 // the status word, skips the remaining work, waits (bounded) for this CTA's copies
 // in flight and frees its tensor memory before returning.
-#include <cuda.h>
-
 #include <algorithm>
-#include <mutex>
 
 #include "gemm.cuh"
+#include "tma.cuh"
 
 namespace b200 {
 namespace {
@@ -339,35 +337,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
 // [rows][cols] F32 matrix with row stride `ld` floats, boxes of [box_rows x 32 floats].
 bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-    const cuuint32_t box[2] = {kTBK, box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
+    const uint32_t box[2] = {static_cast<uint32_t>(kTBK), box_rows};
+    return tma_encode_f32(map, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int EPI, int BN>

@@ -41,7 +41,10 @@ def test_status_strings_and_host_helpers():
     table = oracle.Port().rope_table(1e6, 128, 2)
     assert np.array_equal(f, table[1])
     # workspace queries are pure host arithmetic
-    assert lib.b200_flash_attn_workspace_bytes(128, 16, 8, 1, 8192) == 0  # cluster merge, no scratch
+    # decode: 16 counter words, then 8 KV heads x 18 splits (128 keys each, one CTA per
+    # SM over the KV heads) x 2 query heads x (128 + m + l) floats; prefill needs none
+    assert lib.b200_flash_attn_workspace_bytes(128, 16, 8, 1, 8192) == (16 + 8 * 18 * 2 * 130) * 4
+    assert lib.b200_flash_attn_workspace_bytes(128, 16, 8, 1, 100) == (16 + 8 * 1 * 2 * 130) * 4
     assert lib.b200_argmax_workspace_bytes(151936) >= 256
 
 

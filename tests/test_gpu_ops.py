@@ -121,13 +121,35 @@ def test_flash_attn_decode(cuda, port, L):
 
 
 def test_flash_attn_decode_repeat_reuses_workspace(cuda, port):
-    rng = np.random.default_rng(5)
-    q, k, v = _attn_case(rng, 1, 500)
-    ws = torch.empty(B.lib().b200_flash_attn_workspace_bytes(128, 16, 8, 1, 501), dtype=torch.uint8, device=cuda)
-    want = port.flash_attn(q, k, v, 500, threads=THREADS)
-    for _ in range(3):
-        got = B.flash_attn(T(q, cuda), T(k, cuda), T(v, cuda), 500, workspace=ws).cpu().numpy()
-        assert rel_err(got, want) <= 1e-5
+    """One zero-filled workspace serves repeated calls and other lengths: the split
+    counters are left at zero by every call."""
+    ws = torch.zeros(B.lib().b200_flash_attn_workspace_bytes(128, 16, 8, 1, 8192), dtype=torch.uint8, device=cuda)
+    for n_past in (500, 500, 8191, 37, 4000, 0):
+        rng = np.random.default_rng(n_past + 5)
+        q, k, v = _attn_case(rng, 1, n_past)
+        want = port.flash_attn(q, k, v, n_past, threads=THREADS)
+        got = B.flash_attn(T(q, cuda), T(k, cuda), T(v, cuda), n_past, workspace=ws).cpu().numpy()
+        assert rel_err(got, want) <= 1e-5, n_past
+    assert int(torch.count_nonzero(ws[:4 * 8])) == 0  # the Hkv split counters, at the start
+
+
+@pytest.mark.parametrize("L", [1, 300, 4096])
+def test_flash_attn_decode_without_workspace(cuda, port, L):
+    """No workspace: the cluster-merged decode (at most 16 splits per KV head)."""
+    rng = np.random.default_rng(L + 1)
+    q, k, v = _attn_case(rng, 1, L - 1)
+    none = torch.empty(0, dtype=torch.uint8, device=cuda)
+    got = B.flash_attn(T(q, cuda), T(k, cuda), T(v, cuda), L - 1, workspace=none).cpu().numpy()
+    assert rel_err(got, port.flash_attn(q, k, v, L - 1, threads=THREADS)) <= 1e-5
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(8, 8, 128), (16, 4, 64), (32, 4, 128), (8, 1, 256), (4, 2, 64)])
+@pytest.mark.parametrize("L", [33, 1500])
+def test_flash_attn_decode_gqa_shapes(cuda, port, Hq, Hkv, D, L):
+    rng = np.random.default_rng(Hq * 100 + Hkv * 10 + D + L)
+    q, k, v = _attn_case(rng, 1, L - 1, Hq=Hq, Hkv=Hkv, D=D)
+    got = B.flash_attn(T(q, cuda), T(k, cuda), T(v, cuda), L - 1).cpu().numpy()
+    assert rel_err(got, port.flash_attn(q, k, v, L - 1, threads=THREADS)) <= 1e-5
 
 
 @pytest.mark.parametrize("S", [32, 64, 128, 256, 2048])
