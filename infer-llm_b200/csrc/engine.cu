@@ -13,7 +13,8 @@
 //
 // The decode step reads the token and n_past from device memory and writes the
 // next token back, so it is captured once as a CUDA graph and replayed with no
-// host round trip. Prefill uses the tiled FFMA / tcgen05 GEMMs and the tiled
+// host round trip (under tensor parallelism with the NCCL all-reduces and the
+// token all-gather inside the graph). Prefill uses the tiled FFMA / tcgen05 GEMMs and the tiled
 // attention kernel over all prompt rows and samples from the last row only.
 #include <cmath>
 #include <cstdio>
@@ -743,6 +744,7 @@ void b200_engine_destroy(b200_engine *e) {
     if (!e) return;
     DeviceGuard dg(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    // the decode graph holds NCCL operations under tensor parallelism: released first
     if (e->graph_exec) cudaGraphExecDestroy(e->graph_exec);
     if (e->graph) cudaGraphDestroy(e->graph);
     if (e->tp) tp_destroy(e->tp);
@@ -958,7 +960,9 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
     cudaStream_t st = e->stream;
     const bool want_logits = host_last_logits != nullptr;
     int rc;
-    if (n == 1 && e->c.tp_world == 1 && (!want_logits || e->use_mk)) {
+    // one token: the captured decode step (under tensor parallelism it holds the NCCL
+    // all-reduces and the token all-gather; logits are not returned there)
+    if (n == 1 && (e->c.tp_world > 1 || !want_logits || e->use_mk)) {
         // graph-replayed decode: the token slot is the embedding input
         e->pinned_io[0] = host_ids[0];
         B200_TRY(cudaMemcpyAsync(e->token, e->pinned_io, 4, cudaMemcpyHostToDevice, st));
@@ -995,20 +999,10 @@ int b200_engine_generate(b200_engine *e, int64_t n_steps, int32_t *host_tokens) 
     if (n_steps > e->log_cap) return B200_ERR_INVALID_ARGUMENT;
     DeviceGuard dg(e->device);
     cudaStream_t st = e->stream;
-    int rc = B200_OK;
-    if (e->c.tp_world == 1) {
-        rc = build_graph(e);
-        if (rc != B200_OK) return rc;
-    }
+    int rc = build_graph(e);
+    if (rc != B200_OK) return rc;
     B200_TRY(cudaMemsetAsync(e->log_pos, 0, 4, st));
-    for (int64_t i = 0; i < n_steps; ++i) {
-        if (e->c.tp_world == 1) {
-            B200_TRY(cudaGraphLaunch(e->graph_exec, st));
-        } else {
-            rc = enqueue_small_step(e, e->token, 1, false, 1, true);
-            if (rc != B200_OK) return rc;
-        }
-    }
+    for (int64_t i = 0; i < n_steps; ++i) B200_TRY(cudaGraphLaunch(e->graph_exec, st));
     if (host_tokens && n_steps > 0)
         B200_TRY(cudaMemcpyAsync(host_tokens, e->token_log, n_steps * 4, cudaMemcpyDeviceToHost, st));
     rc = check_status(e);

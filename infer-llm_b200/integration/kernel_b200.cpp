@@ -68,10 +68,24 @@ cudaError_t compute_flash_attn(Tensor *dst, cudaStream_t s) {
     std::memcpy(&p, dst->op_params, sizeof p);
     const int64_t D = q->dims[0];
     const float scale = p.scale > 0.0f ? p.scale : 1.0f / std::sqrt(static_cast<float>(D));
+    // Decode splits merge through a zero-filled workspace that later calls reuse; it
+    // grows with the context (the reference kernel mallocs a score matrix per call,
+    // kernel_f32.cu:484-510). One backend thread drives the stream.
+    static void *ws = nullptr;
+    static size_t ws_bytes = 0;
+    const size_t need = b200_flash_attn_workspace_bytes(D, q->dims[1], k->dims[1], q->dims[2], k->dims[2]);
+    if (need > ws_bytes) {
+        if (ws && cudaFree(ws) != cudaSuccess) return cudaErrorUnknown;
+        ws = nullptr;
+        ws_bytes = 0;
+        if (cudaMalloc(&ws, need) != cudaSuccess) return cudaErrorMemoryAllocation;
+        if (cudaMemsetAsync(ws, 0, need, s) != cudaSuccess) return cudaErrorUnknown;
+        ws_bytes = need;
+    }
     // K / V are views of the cache: token stride strides[2], head stride strides[1] (bytes)
     return as_cuda(b200_flash_attn(cf(q), cf(k), cf(v), mf(dst), D, q->dims[1], k->dims[1], q->dims[2], k->dims[2],
                                    static_cast<int64_t>(p.n_ctx), scale, k->strides[2] / 4, k->strides[1] / 4,
-                                   v->strides[2] / 4, v->strides[1] / 4, nullptr, 0, s));
+                                   v->strides[2] / 4, v->strides[1] / 4, ws, ws_bytes, s));
 }
 
 cudaError_t compute_get_rows(Tensor *dst, cudaStream_t s) {
