@@ -48,6 +48,22 @@ TRAFFIC_PER_STEP = 2_396_254_624
 METRIC = "decode tok/s (Qwen3-0.6B-shape F32 bs1, 32-token prompt, greedy)"
 
 
+_OUT_FD = None  # the process's original stdout: the JSON result lines only
+
+
+def emit(obj) -> None:
+    """Writes one JSON result line to the original stdout. Everything else the
+    process prints, including the reference library's own messages from C++
+    (its CPU backend reports its destructor on stdout at exit), goes to stderr,
+    so stdout carries exactly the result lines."""
+    line = (json.dumps(obj) + "\n").encode()
+    if _OUT_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_OUT_FD, line)
+
+
 def peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -175,7 +191,10 @@ def trace_summary_mk(tr, cfg, sm_mhz=1965.0):
     """Per phase class of one step of the single-launch decode kernel (CTA 0's
     stamps): mean total (phase start to the end of its grid barrier), input load,
     main loop (ring loop + epilogue), barrier wait, the slowest warp's total wait for
-    its weight chunks and the ring loop alone; plus the step's span."""
+    its weight chunks and the ring loop alone; plus the step's span. For attention
+    (CTA 0 is the first split of KV head 0): load = q / k / v exchange with QK-norm
+    and RoPE, loop = scores through the stored split partial, main - loop = the
+    split merge."""
     names = []
     for _ in range(cfg.n_layer):
         names += ["qkv", "attention", "o_proj", "gate_up", "down"]
@@ -359,7 +378,7 @@ def run_b200(args):
     elif world > 1:
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        emit(res)
 
 
 def cpu_baseline(cfg, threads=0, sample_steps=16):
@@ -393,11 +412,11 @@ def run_reference(args):
     from b200infer import gguf as G
     cfg = model_cfg(args.model)
     if args.model != "0.6b":
-        print(json.dumps({"impl": "reference", "unavailable": "the reference CPU path at the 8B shape is only "
-                          "timed for the 0.6B workload"}))
+        emit({"impl": "reference", "unavailable": "the reference CPU path at the 8B shape is only "
+                          "timed for the 0.6B workload"})
         return
     if not oracle.Ref.available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference built from source) missing"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref (reference built from source) missing"})
         return
     threads = args.cpu_threads or (os.cpu_count() or 1)
     ref = oracle.Ref()
@@ -417,7 +436,7 @@ def run_reference(args):
     dt = time.perf_counter() - t1
     eng.close()
     value = steps / dt
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC.replace("32-token", f"{plen}-token"), "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -428,7 +447,7 @@ def run_reference(args):
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
                          "sample": f"{steps} greedy decode tokens after a {plen}-token prefill"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 def run_op(args):
@@ -463,7 +482,7 @@ def run_op(args):
     else:
         cases = [dict(op=args.op, K=args.K, N=args.N, M=args.M, L=args.L, precision=args.precision)]
     for c in cases:
-        print(json.dumps(op_case(c, args.steps, args.warmup)), flush=True)
+        emit(op_case(c, args.steps, args.warmup))
 
 
 def op_case(c, steps, warmup):
@@ -541,6 +560,10 @@ def main():
     ap.add_argument("--decode", choices=["auto", "multi", "single"], default="auto",
                     help="decode step: multi-kernel chain, single-launch kernel, or the engine's choice")
     args = ap.parse_args()
+    global _OUT_FD
+    sys.stdout.flush()
+    _OUT_FD = os.dup(1)  # result lines only; everything else printed goes to stderr
+    os.dup2(2, 1)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.op:
