@@ -51,6 +51,7 @@ constexpr int kPartFloats = 2048;    // per-CTA row sums of one phase
 constexpr int kResFloats = 64;       // this CTA's rows of the residual stream
 constexpr int kMaxSplits = 18;
 constexpr int kDefaultInflight = 8;  // measured: 8 copies (96 KB) per SM keep HBM busy; 3 starve the LM head
+constexpr int kDefaultSplitKeys = 32;  // keys per attention split
 constexpr int kMaxGq = 4;            // query heads per KV head (attention registers)
 enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_PER_LAYER = 5 };
 
@@ -64,6 +65,10 @@ struct PhaseW {
 // phases constantly and every phase starts from a layer pointer, so none of them
 // may wait on a global load to find its matrix or norm weights.
 __shared__ MkLayer s_layers[kMaxLayers];
+// cos / sin of this step's rotation angles (the position is the same in every
+// layer): s_rope[j] = cos, s_rope[kMaxHalfD + j] = sin of float(double(pos) * freq_j).
+constexpr int kMaxHalfD = 64;
+__shared__ float s_rope[2 * kMaxHalfD];
 
 B200_DEVICE PhaseW phase_w(const MkParams &p, int l, int ph) {
     if (l == p.n_layer) return {p.lm_head, p.V, p.H, 1};
@@ -151,6 +156,14 @@ B200_DEVICE float2 ld_keep2(const float *p, uint64_t pol) {
     asm volatile("ld.global.cg.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;" : "=f"(v.x), "=f"(v.y) : "l"(p), "l"(pol));
     return v;
 }
+B200_DEVICE void prefetch_l2_keep(const float *p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+B200_DEVICE float ld_keep_f(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
 B200_DEVICE void st_keep(float *p, float v, uint64_t pol) {
     asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
 }
@@ -209,6 +222,11 @@ B200_DEVICE void st_tagged(u64 *p, float v, uint32_t tag) {
     const u64 w = (static_cast<u64>(tag) << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+B200_DEVICE u64 ld_tagged1(const u64 *p) {
+    u64 a;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+    return a;
+}
 B200_DEVICE void ld_tagged2(const u64 *p, u64 &a, u64 &b) {
     asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
@@ -245,6 +263,11 @@ B200_DEVICE bool poll_pairs(unsigned pending, const int32_t *status_p, int32_t *
     return false;
 }
 
+// Device trace (CTA 0, thread 0): phase idx, slot k <- global time.
+B200_DEVICE void stamp(const MkParams &p, int idx, int k) {
+    if (p.trace && threadIdx.x == 0 && blockIdx.x == 0) p.trace[idx * 8 + k] = global_ns();
+}
+
 struct Smem {
     uint64_t *full, *empty;  // [kStages] copy-complete / slot-read barriers
     float *ring;   // [kStages][kStageFloats]
@@ -270,14 +293,17 @@ struct Mk {
     // flight together, only stale pairs re-read); gamma is applied from shared
     // memory once the sum of squares is known.
     B200_DEVICE bool load_act(const u64 *src, int64_t K, const float *gamma, uint32_t want) {
-        constexpr int kP = 2;  // word pairs per thread per round (register budget)
+        // word pairs per thread per round: the largest input (kMaxK floats) is
+        // requested in one round, so a phase waits one L2 round trip, not K / 512
+        constexpr int kP = kMaxK / 2 / kCT;
         __shared__ double s_red[kCW];
         __shared__ int s_bad;
         if (tid == 0) s_bad = 0;
         const int64_t K2 = K >> 1;
-        float2 gv[kP];  // gamma of the first round, loaded with it
+        constexpr int kG = 2;  // gamma pairs per thread loaded with the words (K <= 2 kG kCT)
+        float2 gv[kG];
 #pragma unroll
-        for (int j = 0; j < kP; ++j)
+        for (int j = 0; j < kG; ++j)
             if (gamma && tid + j * kCT < K2) gv[j] = ld_keep2(gamma + 2 * (tid + j * kCT), keep);
         double ss = 0.0;
         bool ok = true;
@@ -323,10 +349,10 @@ struct Mk {
                 reinterpret_cast<float2 *>(sm.xs)[i] = y;
             };
 #pragma unroll
-            for (int j = 0; j < kP; ++j)
+            for (int j = 0; j < kG; ++j)
                 if (tid + j * kCT < K2) apply(tid + j * kCT, gv[j]);
 #pragma unroll 1
-            for (int64_t i = tid + kP * kCT; i < K2; i += kCT) apply(i, ld_keep2(gamma + 2 * i, keep));
+            for (int64_t i = tid + kG * kCT; i < K2; i += kCT) apply(i, ld_keep2(gamma + 2 * i, keep));
         }
         named_sync(1, kCT);
         return s_bad == 0;  // uniform over the CTA
@@ -486,10 +512,10 @@ struct Mk {
 
     B200_DEVICE float row_sum(int64_t lr) const { return sm.part[lr]; }
 
-    // Attention splits per KV head for L keys: about 32 keys per split, at most
+    // Attention splits per KV head for L keys: about p.split_keys keys per split, at most
     // kMaxSplits and at most G / Hkv (one CTA per (KV head, split)).
     B200_DEVICE int attn_splits(int64_t L) const {
-        const int S = static_cast<int>((L + 31) / 32);
+        const int S = static_cast<int>((L + p.split_keys - 1) / p.split_keys);
         return max(1, min(S, min(kMaxSplits, G / p.Hkv)));
     }
 
@@ -514,11 +540,10 @@ struct Mk {
     // rounding: float squares summed in double, y = (x * scale) * gamma, angle =
     // float(double(pos) * freq_j), separately rounded rotation products). The head
     // comes from tagged words; gamma and the frequency table are loaded with it.
-    B200_DEVICE bool norm_rope_head(const u64 *src, uint32_t want, const float *gamma, int64_t pos, float *dst) {
+    B200_DEVICE bool norm_rope_head(const u64 *src, uint32_t want, const float *gamma, float *dst) {
         const bool lo = lane < 16;
-        float v[E], gm[E], fr[E];
+        float v[E], gm[E];
         ld_keep_vec(gamma + lane * E, gm, keep);
-        ld_keep_vec(p.freq + (lo ? lane : lane - 16) * E, fr, keep);
         const bool ok = read_head_lane(src, want, v);
         double ss = 0.0;
 #pragma unroll
@@ -533,16 +558,29 @@ struct Mk {
         float other[E];
 #pragma unroll
         for (int e = 0; e < E; ++e) other[e] = __shfl_xor_sync(0xffffffffu, v[e], 16);
-        // one copy of the accurate sincosf (its large-argument path is big)
-#pragma unroll 1
+        const int j0 = (lo ? lane : lane - 16) * E;
+#pragma unroll
         for (int e = 0; e < E; ++e) {
-            const float ang = static_cast<float>(static_cast<double>(pos) * static_cast<double>(fr[e]));
-            float s, c;
-            sincosf(ang, &s, &c);
+            const float c = s_rope[j0 + e], s = s_rope[kMaxHalfD + j0 + e];
             dst[lane * E + e] = lo ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other[e], s))
                                    : __fadd_rn(__fmul_rn(other[e], s), __fmul_rn(v[e], c));
         }
         return __all_sync(0xffffffffu, ok);
+    }
+
+    // The step's rotation table (every layer rotates at the same position n_past):
+    // the reference's table entry float(double(pos) * freq_j), then its sine and
+    // cosine, once per launch instead of once per head and layer.
+    B200_DEVICE void rope_table(int64_t pos) {
+        // one copy of the accurate sincosf (its large-argument path is big)
+#pragma unroll 1
+        for (int j = tid; j < D / 2; j += kCT) {
+            const float ang = static_cast<float>(static_cast<double>(pos) * static_cast<double>(ld_keep_f(p.freq + j)));
+            float sn, cs;
+            sincosf(ang, &sn, &cs);
+            s_rope[j] = cs;
+            s_rope[kMaxHalfD + j] = sn;
+        }
     }
 
     // ---- attention for one (KV head g, split s): the split's keys are cut into
@@ -587,11 +625,24 @@ struct Mk {
             }
         };
         load_batch(t0, static_cast<int>(min64(kTB, t1 - t0)));
+        {
+            // the next kPreB batches' cached rows towards L2 meanwhile (the first
+            // batch is in flight to registers): E lines of 128 B per row
+            constexpr int kPreB = 3;
+            const int64_t nk = min64(kPreB * kTB, max64(0, t1 - t0 - kTB));
+            const float *kr = Lw.kc + g * D, *vr = Lw.vc + g * D;
+#pragma unroll 1
+            for (int64_t x = lane; x < nk * 2 * E; x += 32) {
+                const int64_t key = t0 + kTB + x / (2 * E);
+                const int line = static_cast<int>(x % E);
+                prefetch_l2_keep(((x / E) & 1 ? vr : kr) + key * tok + line * 32);
+            }
+        }
         bool ok = true;
         const bool isq = warp < Gq, isk = last && warp == Gq;
         if (isq || isk) {  // one call site for the norm + RoPE code
             ok = norm_rope_head(p.tqkv + (isq ? g * Gq + warp : p.Hq + g) * D, want, isq ? Lw.q_norm : Lw.k_norm,
-                                n_past, isq ? sm.qs + warp * D : kn);
+                                isq ? sm.qs + warp * D : kn);
             if (isk) {
                 __syncwarp();
                 float *dst = Lw.kc + n_past * tok + g * D;
@@ -612,6 +663,8 @@ struct Mk {
         if (!ok && lane == 0) s_bad = 1;
         named_sync(1, kCT);
         if (s_bad) return false;
+        const int tq = layer * PH_PER_LAYER + PH_ATTN;
+        stamp(p, tq, 4);  // q / k / v in, normalised and rotated
         float q[kMaxGq][E], m[kMaxGq], l[kMaxGq], o[kMaxGq][E];
 #pragma unroll
         for (int hh = 0; hh < kMaxGq; ++hh) {
@@ -695,6 +748,8 @@ struct Mk {
         }
         named_sync(1, kCT);
         // merge the kCW sub-ranges of each head in order -> the split's partial
+        // (or, with one split, the group's output: os / lsum is what the split
+        // merge below yields for S == 1, exp(0) and fmaf(1, x, 0) being exact)
 #pragma unroll 1
         for (int i = tid; i < Gq * D; i += kCT) {
             const int hh = i / D, d = i % D;
@@ -710,6 +765,10 @@ struct Mk {
                 lsum = fmaf(f, w[D + 1], lsum);
                 os = fmaf(f, w[d], os);
             }
+            if (S == 1) {
+                st_tagged(p.tao + static_cast<int64_t>(g * Gq) * D + i, os / lsum, mine);
+                continue;
+            }
             const int64_t sh = static_cast<int64_t>(s) * p.Hq + g * Gq + hh;
             st_tagged(p.tpo + sh * D + d, os, mine);
             if (d == 0) {
@@ -717,127 +776,88 @@ struct Mk {
                 st_tagged(p.tpml + sh * 2 + 1, lsum, mine);
             }
         }
-        named_sync(1, kCT);  // sm.xs (the partials) is read before the o_proj input overwrites it
-        return true;
+        named_sync(1, kCT);  // sm.xs (the sub-range partials) is read before it is reused
+        stamp(p, tq, 7);  // split partial stored
+        return S == 1 || merge_group(layer, g, s, S);
     }
 
-    // ---- o_proj input: merge the attention splits (split order) into xs. Every
-    // split's (m, l) and the first kSG splits' partial outputs are requested
-    // together (one L2 round trip for S <= kSG), the split weights are formed from
-    // (m, l), then per thread its word pairs of the next kSG splits at a time.
-    B200_DEVICE bool merge_attention(int layer, int64_t n_past) {
-        constexpr int kP = 4;   // word pairs per thread: Hq * D <= 2 * kP * kCT
-        constexpr int kSG = 2;  // splits loaded per round (register budget)
-        constexpr int kM = 2;   // (split, head) pairs per thread: kMaxSplits * Hq <= kM * kCT
+    // ---- split merge inside the attention CTAs: CTA (g, s) merges its slice
+    // [n s / S, n (s + 1) / S) of the n = Gq D outputs of KV group g from the S
+    // split partials (one round of word loads: every split's value of the slice
+    // and every split's (max, sum) of the group's heads), in split order, and
+    // writes the merged outputs as tagged words. The o_proj phase then reads the
+    // Hq D outputs in one round instead of S partials in several.
+    B200_DEVICE bool merge_group(int layer, int g, int s, int S) {
+        constexpr int kW = 3;  // slice words per thread: S * ns <= n + S <= kW * kCT
         const uint32_t want = tag(layer, PH_ATTN);
-        const int S = attn_splits(n_past + 1);
-        const int Hq = p.Hq;
-        const int n2 = Hq * D / 2;
-        float *sw = sm.part;                      // [S][Hq]: m, then the split weight
-        float *sl = sm.part + kMaxSplits * Hq;    // [S][Hq]: l
-        float *sden = sl + kMaxSplits * Hq;       // [Hq]: sum of weighted l
+        const int Gq = p.Hq / p.Hkv, n = Gq * D;
+        const int e0 = n * s / S, e1 = n * (s + 1) / S, ns = e1 - e0;
+        float *vals = sm.xs;            // [S][ns]
+        float *ml = sm.xs + kMaxK / 2;  // [S][Gq][2]
         __shared__ int s_bad;
         if (tid == 0) s_bad = 0;
-        named_sync(1, kCT);
-        u64 oa[kSG * kP], oc[kSG * kP];  // one round of partial-output pairs
-        unsigned opend = 0;
-        auto issue = [&](int s0) {
-            opend = 0;
-#pragma unroll
-            for (int j = 0; j < kSG; ++j)
-#pragma unroll
-                for (int v = 0; v < kP; ++v) {
-                    const int i2 = tid + v * kCT;
-                    if (s0 + j < S && i2 < n2) {
-                        ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + i2) * 2, oa[j * kP + v], oc[j * kP + v]);
-                        opend |= 1u << (j * kP + v);
-                    }
-                }
+        auto word = [&](int j) -> const u64 * {  // slice word j = (split, element)
+            const int sp = j / ns, i = j % ns;
+            return p.tpo + (static_cast<int64_t>(sp) * p.Hq + g * Gq) * D + e0 + i;
         };
-        bool ok = true;
-        {
-            u64 a[kM], c[kM];
-            unsigned pending = 0;
+        u64 w[kW], ma = 0, mb = 0;
+        unsigned pending = 0;
 #pragma unroll
-            for (int j = 0; j < kM; ++j) {
-                const int i = tid + j * kCT;
-                if (i < S * Hq) {
-                    ld_tagged2(p.tpml + 2 * i, a[j], c[j]);
-                    pending |= 1u << j;
-                }
+        for (int k = 0; k < kW; ++k) {
+            const int j = tid + k * kCT;
+            if (j < S * ns) {
+                w[k] = ld_tagged1(word(j));
+                pending |= 1u << k;
             }
-            issue(0);  // in flight while (m, l) is polled and the weights are formed
-            ok = poll_pairs<kM>(
-                pending, p.status, p.status, [&](int j) { return tag_hi(a[j]) == want && tag_hi(c[j]) == want; },
-                [&](int j) { ld_tagged2(p.tpml + 2 * (tid + j * kCT), a[j], c[j]); });
+        }
+        const bool has_ml = tid < S * Gq;  // (split, head) = (tid / Gq, tid % Gq)
+        auto ml_src = [&]() { return p.tpml + (static_cast<int64_t>(tid / Gq) * p.Hq + g * Gq + tid % Gq) * 2; };
+        if (has_ml) {
+            ld_tagged2(ml_src(), ma, mb);
+            pending |= 1u << kW;
+        }
+        const bool ok = poll_pairs<kW + 1>(
+            pending, p.status, p.status,
+            [&](int k) { return k < kW ? tag_hi(w[k]) == want : (tag_hi(ma) == want && tag_hi(mb) == want); },
+            [&](int k) {
+                if (k < kW)
+                    w[k] = ld_tagged1(word(tid + k * kCT));
+                else
+                    ld_tagged2(ml_src(), ma, mb);
+            });
 #pragma unroll
-            for (int j = 0; j < kM; ++j)
-                if ((pending >> j) & 1u) {
-                    sw[tid + j * kCT] = tag_val(a[j]);
-                    sl[tid + j * kCT] = tag_val(c[j]);
-                }
+        for (int k = 0; k < kW; ++k)
+            if ((pending >> k) & 1u) vals[tid + k * kCT] = tag_val(w[k]);
+        if (has_ml) {
+            ml[2 * tid] = tag_val(ma);
+            ml[2 * tid + 1] = tag_val(mb);
         }
         if (!ok) s_bad = 1;
         named_sync(1, kCT);
         if (s_bad) return false;
+        const uint32_t mine = tag(layer, PH_ATTN);
 #pragma unroll 1
-        for (int hh = tid; hh < Hq; hh += kCT) {
+        for (int i = tid; i < ns; i += kCT) {
+            const int hh = (e0 + i) / D;
             float M = -INFINITY;
 #pragma unroll 1
-            for (int s = 0; s < S; ++s) M = fmaxf(M, sw[s * Hq + hh]);
-            float lsum = 0.f;
+            for (int sp = 0; sp < S; ++sp) M = fmaxf(M, ml[2 * (sp * Gq + hh)]);
+            float lsum = 0.f, acc = 0.f;
 #pragma unroll 1
-            for (int s = 0; s < S; ++s) {
-                const float ms = sw[s * Hq + hh];
+            for (int sp = 0; sp < S; ++sp) {
+                const float ms = ml[2 * (sp * Gq + hh)];
                 const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
-                if (ms != -INFINITY) lsum = fmaf(f, sl[s * Hq + hh], lsum);
-                sw[s * Hq + hh] = f;
+                if (ms != -INFINITY) lsum = fmaf(f, ml[2 * (sp * Gq + hh) + 1], lsum);
+                acc = fmaf(f, vals[sp * ns + i], acc);
             }
-            sden[hh] = lsum;
+            st_tagged(p.tao + static_cast<int64_t>(g * Gq) * D + e0 + i, acc / lsum, mine);
         }
-        named_sync(1, kCT);
-        float2 acc[kP];
-#pragma unroll
-        for (int v = 0; v < kP; ++v) acc[v] = make_float2(0.f, 0.f);
-#pragma unroll 1
-        for (int s0 = 0; s0 < S && ok; s0 += kSG) {
-            if (s0) issue(s0);
-            ok = poll_pairs<kSG * kP>(
-                opend, p.status, p.status,
-                [&](int q) { return tag_hi(oa[q]) == want && tag_hi(oc[q]) == want; },
-                [&](int q) {
-                    const int j = q / kP, v = q % kP;
-                    ld_tagged2(p.tpo + (static_cast<int64_t>(s0 + j) * n2 + tid + v * kCT) * 2, oa[q], oc[q]);
-                });
-#pragma unroll
-            for (int j = 0; j < kSG; ++j)
-#pragma unroll
-                for (int v = 0; v < kP; ++v) {
-                    const int i2 = tid + v * kCT;
-                    if (s0 + j < S && i2 < n2) {
-                        const float f = sw[(s0 + j) * Hq + i2 * 2 / D];
-                        acc[v].x = fmaf(f, tag_val(oa[j * kP + v]), acc[v].x);
-                        acc[v].y = fmaf(f, tag_val(oc[j * kP + v]), acc[v].y);
-                    }
-                }
-        }
-        if (!ok) s_bad = 1;
-#pragma unroll
-        for (int v = 0; v < kP; ++v) {
-            const int i2 = tid + v * kCT;
-            if (i2 < n2) {
-                const float den = sden[i2 * 2 / D];
-                reinterpret_cast<float2 *>(sm.xs)[i2] = make_float2(acc[v].x / den, acc[v].y / den);
-            }
-        }
-        named_sync(1, kCT);
-        return s_bad == 0;
+        named_sync(1, kCT);  // sm.xs is read before the o_proj input overwrites it
+        return true;
     }
+
 };
 
-B200_DEVICE void stamp(const MkParams &p, int idx, int k) {
-    if (p.trace && threadIdx.x == 0 && blockIdx.x == 0) p.trace[idx * 8 + k] = global_ns();
-}
 
 template <int D>
 B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p);
@@ -951,6 +971,8 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
 #pragma unroll 1
         for (int64_t r = r0 + tid; r < r1; r += kCT) mk.sm.res[r - r0] = __ldg(emb + r);
     }
+    mk.rope_table(ok ? n_past : 0);
+    named_sync(1, kCT);
     // One pass over the step's phases (per layer QKV, attention, o_proj, gate/up,
     // down; then the LM head), each helper called from exactly one place so that
     // the kernel's code stays small enough for the instruction cache.
@@ -968,7 +990,7 @@ B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
         rows_of(pw.N, pw.unit, b, G, r0, r1);
         // phase input
         if (ph == PH_O) {
-            ok = mk.merge_attention(l, n_past);
+            ok = mk.load_act(p.tao, static_cast<int64_t>(p.Hq) * p.D, nullptr, mk.tag(l, PH_ATTN));
         } else if (q == 0) {
             mk.load_act_plain(emb, p.H, s_layers[0].attn_norm);
         } else {
@@ -1117,6 +1139,17 @@ int mk_max_inflight() {
     return v;
 }
 
+// Keys per attention split (B200_MK_SPLIT_KEYS overrides the default).
+int mk_split_keys() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = std::getenv("B200_MK_SPLIT_KEYS");
+        const int x = (e && *e) ? std::atoi(e) : kDefaultSplitKeys;
+        v = std::min(std::max(x, 8), 1024);
+    }
+    return v;
+}
+
 int mk_max_splits() { return kMaxSplits; }
 size_t mk_po_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * p.D; }
 size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) * p.Hq * 2; }
@@ -1134,9 +1167,11 @@ bool mk_supported(const MkParams &p) {
     const int64_t nmax = std::max<int64_t>({static_cast<int64_t>(p.V), 2 * static_cast<int64_t>(p.F),
                                             static_cast<int64_t>(p.Hq + 2 * p.Hkv) * p.D});
     if (nmax * (G + 1) >= (1LL << 32)) return false;
-    // merge: scratch in sm.part, (split, head) pairs and output pairs per thread
-    if (2 * kMaxSplits * p.Hq + p.Hq > kPartFloats || kMaxSplits * p.Hq > 2 * kCT || p.Hq * p.D > 8 * kCT)
-        return false;
+    // split merge in the attention CTAs (merge_group): one (split, head) pair and
+    // kW = 3 slice words per thread; scratch in sm.xs
+    const int Gq = p.Hq / p.Hkv;
+    if (kMaxSplits * Gq > kCT || Gq * p.D + kMaxSplits > 3 * kCT || 2 * kMaxSplits * Gq > kMaxK / 2) return false;
+    if (p.D / 2 > kMaxHalfD) return false;
     const int64_t Ks[] = {p.H, static_cast<int64_t>(p.Hq) * p.D, p.F};
     for (int64_t K : Ks)
         if (K > kMaxK || (K & 3) || K < 64) return false;
@@ -1161,6 +1196,7 @@ cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     MkParams args = p;
     args.max_inflight = mk_max_inflight();
+    args.split_keys = mk_split_keys();
     void *kargs[] = {&args};
     return cudaLaunchCooperativeKernel(kern, dim3(mk_grid()), dim3(kThreads), kargs, smem, stream);
 }

@@ -25,6 +25,7 @@ struct MkParams {
     unsigned long long *th = nullptr;    // SwiGLU output [F]
     unsigned long long *tpo = nullptr;   // attention split partial outputs [max_splits][Hq][D]
     unsigned long long *tpml = nullptr;  // attention split (max, sum) [max_splits][Hq][2]
+    unsigned long long *tao = nullptr;   // merged attention output [Hq][D]
     unsigned *launches = nullptr;        // + gridDim.x per launch: the tag base (zero at create)
     float *logits = nullptr;           // [V] or nullptr
     int32_t *token = nullptr;          // in: token of this step; out: greedy next token
@@ -37,6 +38,7 @@ struct MkParams {
     unsigned *am_counter = nullptr;    // zero at launch; the last CTA re-zeroes it
     unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
     int max_inflight = 16;             // ring copies outstanding per CTA (set by mk_launch)
+    int split_keys = 32;               // keys per attention split (set by mk_launch)
 };
 
 // True if the megakernel supports this model shape on this device.
@@ -49,5 +51,6 @@ size_t mk_pml_words(const MkParams &p);
 cudaError_t mk_launch(const MkParams &p, cudaStream_t stream);
 int mk_grid();
 int mk_max_inflight();
+int mk_split_keys();
 
 }  // namespace b200

@@ -656,6 +656,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t o_th = take(2 * F);
     const size_t o_tpo = take(2 * static_cast<int64_t>(mk_po_words(shape)));
     const size_t o_tpml = take(2 * static_cast<int64_t>(mk_pml_words(shape)));
+    const size_t o_tao = take(2 * static_cast<int64_t>(e->Hq) * D);
     const size_t o_mkl_n = take(64);
     e->act_bytes = off;
 
@@ -718,6 +719,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->mk.th = aw(o_th);
     e->mk.tpo = aw(o_tpo);
     e->mk.tpml = aw(o_tpml);
+    e->mk.tao = aw(o_tao);
     e->mk.launches = reinterpret_cast<unsigned *>(e->act_arena + o_mkl_n);
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
