@@ -277,7 +277,9 @@ struct Smem {
     float *res;    // [kResFloats] this CTA's residual rows (o_proj / down row range)
 };
 
-template <int D>
+// D: head_dim; GQ: query heads per KV head (compile time: the attention's per-head
+// loops and warp shuffles then have no head conditions, so they pipeline).
+template <int D, int GQ>
 struct Mk {
     static constexpr int E = D / 32;  // head elements per lane
     const MkParams &p;
@@ -596,7 +598,7 @@ struct Mk {
         constexpr int kTB = 4;
         const MkLayer &Lw = s_layers[layer];
         const uint32_t want = tag(layer, PH_QKV), mine = tag(layer, PH_ATTN);
-        const int Gq = p.Hq / p.Hkv;
+        constexpr int Gq = GQ;
         const int64_t L = n_past + 1;
         const int S = attn_splits(L);
         if (b >= p.Hkv * S) return true;
@@ -665,14 +667,14 @@ struct Mk {
         if (s_bad) return false;
         const int tq = layer * PH_PER_LAYER + PH_ATTN;
         stamp(p, tq, 4);  // q / k / v in, normalised and rotated
-        float q[kMaxGq][E], m[kMaxGq], l[kMaxGq], o[kMaxGq][E];
+        float q[Gq][E], m[Gq], l[Gq], o[Gq][E];
 #pragma unroll
-        for (int hh = 0; hh < kMaxGq; ++hh) {
+        for (int hh = 0; hh < Gq; ++hh) {
             m[hh] = -INFINITY;
             l[hh] = 0.f;
 #pragma unroll
             for (int e = 0; e < E; ++e) {
-                q[hh][e] = hh < Gq ? sm.qs[hh * D + lane * E + e] : 0.f;
+                q[hh][e] = sm.qs[hh * D + lane * E + e];
                 o[hh][e] = 0.f;
             }
         }
@@ -693,11 +695,11 @@ struct Mk {
                         }
                     }
             }
-            float sc[kTB][kMaxGq];
+            float sc[kTB][Gq];
 #pragma unroll
             for (int j = 0; j < kTB; ++j)
 #pragma unroll
-                for (int hh = 0; hh < kMaxGq; ++hh) {
+                for (int hh = 0; hh < Gq; ++hh) {
                     float d = 0.f;
 #pragma unroll
                     for (int e = 0; e < E; ++e) d = fmaf(q[hh][e], kv[j][e], d);
@@ -708,11 +710,10 @@ struct Mk {
 #pragma unroll
                 for (int j = 0; j < kTB; ++j)
 #pragma unroll
-                    for (int hh = 0; hh < kMaxGq; ++hh)
-                        if (hh < Gq) sc[j][hh] += __shfl_xor_sync(0xffffffffu, sc[j][hh], off);
+                    for (int hh = 0; hh < Gq; ++hh)
+                        sc[j][hh] += __shfl_xor_sync(0xffffffffu, sc[j][hh], off);
 #pragma unroll
-            for (int hh = 0; hh < kMaxGq; ++hh) {
-                if (hh >= Gq) continue;
+            for (int hh = 0; hh < Gq; ++hh) {
                 float bm = m[hh];
 #pragma unroll
                 for (int j = 0; j < kTB; ++j) {
@@ -724,20 +725,17 @@ struct Mk {
 #pragma unroll
                 for (int e = 0; e < E; ++e) o[hh][e] *= corr;
 #pragma unroll
-                for (int j = 0; j < kTB; ++j) {
-                    if (j < n) {
-                        const float pr = expf(sc[j][hh] - bm);
-                        l[hh] += pr;
+                for (int j = 0; j < kTB; ++j) {  // keys past n: score -inf, weight 0, v 0
+                    const float pr = expf(sc[j][hh] - bm);
+                    l[hh] += pr;
 #pragma unroll
-                        for (int e = 0; e < E; ++e) o[hh][e] = fmaf(pr, vv[j][e], o[hh][e]);
-                    }
+                    for (int e = 0; e < E; ++e) o[hh][e] = fmaf(pr, vv[j][e], o[hh][e]);
                 }
                 m[hh] = bm;
             }
         }
 #pragma unroll
-        for (int hh = 0; hh < kMaxGq; ++hh) {
-            if (hh >= Gq) continue;
+        for (int hh = 0; hh < Gq; ++hh) {
             float *wp = wpart + (warp * Gq + hh) * (D + 2);
 #pragma unroll
             for (int e = 0; e < E; ++e) wp[lane * E + e] = o[hh][e];
@@ -790,7 +788,8 @@ struct Mk {
     B200_DEVICE bool merge_group(int layer, int g, int s, int S) {
         constexpr int kW = 3;  // slice words per thread: S * ns <= n + S <= kW * kCT
         const uint32_t want = tag(layer, PH_ATTN);
-        const int Gq = p.Hq / p.Hkv, n = Gq * D;
+        constexpr int Gq = GQ;
+        const int n = Gq * D;
         const int e0 = n * s / S, e1 = n * (s + 1) / S, ns = e1 - e0;
         float *vals = sm.xs;            // [S][ns]
         float *ml = sm.xs + kMaxK / 2;  // [S][Gq][2]
@@ -859,8 +858,8 @@ struct Mk {
 };
 
 
-template <int D>
-B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p);
+template <int D, int GQ>
+B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p);
 
 // The producer thread: streams the step's weight schedule through the ring (slot
 // c % kStages for chunk c, refilled as soon as its consumer warp releases it). It
@@ -902,7 +901,7 @@ B200_DEVICE void produce(const MkParams &p, const Smem &sm, int b, int G) {
     for (int c = max(0, cc - kStages); c < cc; ++c) mbar_wait_bounded(&sm.full[c % kStages], (c / kStages) & 1, nullptr);
 }
 
-template <int D>
+template <int D, int GQ>
 __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ uint32_t s_tag0;
@@ -943,12 +942,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
         return;
     }
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
-    Mk<D> mk{p, sm, tid, warp, lane, b, G, s_tag0};
-    run_step<D>(mk, p);
+    Mk<D, GQ> mk{p, sm, tid, warp, lane, b, G, s_tag0};
+    run_step<D, GQ>(mk, p);
 }
 
-template <int D>
-B200_DEVICE void run_step(Mk<D> &mk, const MkParams &p) {
+template <int D, int GQ>
+B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
     const int tid = mk.tid, warp = mk.warp, lane = mk.lane, b = mk.b, G = mk.G;
     int cc = 0;
     const int64_t n_past = *p.n_past;
@@ -1128,6 +1127,16 @@ size_t smem_bytes(int D) {
 
 int mk_grid() { return device_sm_count(); }
 
+// The instantiated (head_dim, query heads per KV head) pairs: the Qwen3 shapes
+// (head_dim 128 with 1, 2 or 4 query heads per KV head) and head_dim 64 with 2.
+static void *mk_kernel(int D, int gq) {
+    if (D == 128 && gq == 1) return reinterpret_cast<void *>(decode_mk_kernel<128, 1>);
+    if (D == 128 && gq == 2) return reinterpret_cast<void *>(decode_mk_kernel<128, 2>);
+    if (D == 128 && gq == 4) return reinterpret_cast<void *>(decode_mk_kernel<128, 4>);
+    if (D == 64 && gq == 2) return reinterpret_cast<void *>(decode_mk_kernel<64, 2>);
+    return nullptr;
+}
+
 // Ring copies in flight per CTA (B200_MK_INFLIGHT overrides the default).
 int mk_max_inflight() {
     static int v = -1;
@@ -1157,7 +1166,7 @@ size_t mk_pml_words(const MkParams &p) { return static_cast<size_t>(kMaxSplits) 
 bool mk_supported(const MkParams &p) {
     if (p.D != 64 && p.D != 128) return false;
     if (p.n_layer < 1 || p.n_layer > kMaxLayers) return false;
-    if (p.Hkv <= 0 || p.Hq % p.Hkv || p.Hq / p.Hkv > kMaxGq) return false;
+    if (p.Hkv <= 0 || p.Hq % p.Hkv || !mk_kernel(p.D, p.Hq / p.Hkv)) return false;
     // attention scratch: kCW x Gq sub-range partials in xs + part below the new k/v
     if (kCW * (p.Hq / p.Hkv) * (p.D + 2) > kMaxK + kPartFloats - 2 * p.D) return false;
     const int G = mk_grid();
@@ -1190,7 +1199,8 @@ bool mk_supported(const MkParams &p) {
 
 cudaError_t mk_launch(const MkParams &p, cudaStream_t stream) {
     const size_t smem = smem_bytes(p.D);
-    void *kern = p.D == 64 ? reinterpret_cast<void *>(decode_mk_kernel<64>) : reinterpret_cast<void *>(decode_mk_kernel<128>);
+    void *kern = p.Hkv > 0 ? mk_kernel(p.D, p.Hq / p.Hkv) : nullptr;
+    if (!kern) return cudaErrorInvalidValue;
     // Per device and cheap: the launch is recorded once into the decode graph.
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
