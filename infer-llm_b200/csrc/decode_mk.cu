@@ -418,17 +418,7 @@ struct Mk {
         float4 a[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) a[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-        for (int i0 = lane; i0 < K4; i0 += 32 * U) {
-            float4 xv[U], wv[R][U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = i0 + 32 * u;
-                xv[u] = i < K4 ? lds4(x_sa + 16u * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int r = 0; r < R; ++r)
-                    wv[r][u] = i < K4 ? lds4(w_sa + 16u * (r * K4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+        auto fma_block = [&](const float4 (&xv)[U], const float4 (&wv)[R][U]) {
 #pragma unroll
             for (int u = 0; u < U; ++u)
 #pragma unroll
@@ -438,6 +428,34 @@ struct Mk {
                     a[r].z = fmaf(wv[r][u].z, xv[u].z, a[r].z);
                     a[r].w = fmaf(wv[r][u].w, xv[u].w, a[r].w);
                 }
+        };
+        // whole blocks of 32 U columns: the loads carry no bounds conditions, so
+        // they issue back to back in one basic block (every projection of the
+        // supported shapes is whole blocks); a ragged tail block after them
+        const int full = K4 / (32 * U) * (32 * U);
+        int i0 = lane;
+#pragma unroll 1
+        for (; i0 < full; i0 += 32 * U) {
+            float4 xv[U], wv[R][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                xv[u] = lds4(x_sa + 16u * (i0 + 32 * u));
+#pragma unroll
+                for (int r = 0; r < R; ++r) wv[r][u] = lds4(w_sa + 16u * (r * K4 + i0 + 32 * u));
+            }
+            fma_block(xv, wv);
+        }
+        if (i0 < K4) {
+            float4 xv[U], wv[R][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + 32 * u;
+                xv[u] = i < K4 ? lds4(x_sa + 16u * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    wv[r][u] = i < K4 ? lds4(w_sa + 16u * (r * K4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            fma_block(xv, wv);
         }
         float acc[R];
 #pragma unroll
