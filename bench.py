@@ -42,9 +42,9 @@ for _p in (os.path.join(REPO, "infer-llm_b200"), os.path.join(REPO, "oracle")):
 PROMPT_LEN = 32
 SEED = 0
 # DRAM bytes (read + write) of one decode_mk_kernel launch, from an ncu --set full
-# capture of `bench.py --steps 4 --warmup 3` (positions ~35; the per-step KV read
+# capture of `bench.py --steps 4 --warmup 3` (positions ~36; the per-step KV read
 # grows by 229,376 bytes per position, weights are 2,384,199,680 of it).
-TRAFFIC_PER_STEP = 2_396_254_624
+TRAFFIC_PER_STEP = 2_395_436_000
 METRIC = "decode tok/s (Qwen3-0.6B-shape F32 bs1, 32-token prompt, greedy)"
 
 
