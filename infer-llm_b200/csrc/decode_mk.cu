@@ -263,6 +263,23 @@ B200_DEVICE bool poll_pairs(unsigned pending, const int32_t *status_p, int32_t *
     return false;
 }
 
+// Named barrier over `threads` threads that also ORs `pred` over them: every
+// participant gets the same answer, so a decision taken on it is uniform over the
+// CTA (a flag in shared memory set by some threads and cleared by one would need
+// a barrier between the clear and the sets).
+B200_DEVICE bool named_sync_or(int id, int threads, bool pred) {
+    int r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n"
+        " setp.ne.s32 p, %1, 0;\n"
+        " bar.red.or.pred q, %2, %3, p;\n"
+        " selp.s32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(pred ? 1 : 0), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 // Device trace (CTA 0, thread 0): phase idx, slot k <- global time.
 B200_DEVICE void stamp(const MkParams &p, int idx, int k) {
     if (p.trace && threadIdx.x == 0 && blockIdx.x == 0) p.trace[idx * 8 + k] = global_ns();
@@ -299,8 +316,6 @@ struct Mk {
         // requested in one round, so a phase waits one L2 round trip, not K / 512
         constexpr int kP = kMaxK / 2 / kCT;
         __shared__ double s_red[kCW];
-        __shared__ int s_bad;
-        if (tid == 0) s_bad = 0;
         const int64_t K2 = K >> 1;
         constexpr int kG = 2;  // gamma pairs per thread loaded with the words (K <= 2 kG kCT)
         float2 gv[kG];
@@ -335,7 +350,6 @@ struct Mk {
                 }
             }
         }
-        if (!ok) s_bad = 1;
         if (gamma) {
             ss = warp_sum(ss);
             if (lane == 0) s_red[warp] = ss;
@@ -356,8 +370,7 @@ struct Mk {
 #pragma unroll 1
             for (int64_t i = tid + kG * kCT; i < K2; i += kCT) apply(i, ld_keep2(gamma + 2 * i, keep));
         }
-        named_sync(1, kCT);
-        return s_bad == 0;  // uniform over the CTA
+        return !named_sync_or(1, kCT, !ok);  // uniform over the CTA
     }
 
     // ---- the same from plain floats (the token's embedding row).
@@ -811,8 +824,6 @@ struct Mk {
         const int e0 = n * s / S, e1 = n * (s + 1) / S, ns = e1 - e0;
         float *vals = sm.xs;            // [S][ns]
         float *ml = sm.xs + kMaxK / 2;  // [S][Gq][2]
-        __shared__ int s_bad;
-        if (tid == 0) s_bad = 0;
         auto word = [&](int j) -> const u64 * {  // slice word j = (split, element)
             const int sp = j / ns, i = j % ns;
             return p.tpo + (static_cast<int64_t>(sp) * p.Hq + g * Gq) * D + e0 + i;
@@ -849,9 +860,7 @@ struct Mk {
             ml[2 * tid] = tag_val(ma);
             ml[2 * tid + 1] = tag_val(mb);
         }
-        if (!ok) s_bad = 1;
-        named_sync(1, kCT);
-        if (s_bad) return false;
+        if (named_sync_or(1, kCT, !ok)) return false;
         const uint32_t mine = tag(layer, PH_ATTN);
 #pragma unroll 1
         for (int i = tid; i < ns; i += kCT) {
@@ -1047,7 +1056,9 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
         stamp(p, q, 5);
         stamp(p, q, 2);
     }
-    if (!ok || status_set(p.status)) return;
+    // uniform: threads that read the status word at different times must not
+    // split between returning and the argmax's barriers below
+    if (named_sync_or(1, kCT, !ok || status_set(p.status) != 0)) return;
     const int lm = p.n_layer * PH_PER_LAYER;
 
     // ---- LM head greedy argmax over the row sums (first maximum; NaN / +inf -> -1)
