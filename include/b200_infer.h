@@ -260,6 +260,14 @@ int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *u
  * < 0. The step leaves n_past and the token unchanged. */
 int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int max_kernels);
 
+/* Failure injection for tests of the single-launch decode step (no counterpart in
+ * the reference): from the next decode step on, CTA `cta` of the step does not
+ * publish its layer-0 QKV outputs, as if it had stopped; the CTAs waiting for them
+ * give up after their bounded wait (2 s), the step returns B200_ERR_TIMEOUT and
+ * commits nothing, and the engine stays usable. cta < 0 ends the injection.
+ * B200_ERR_NOT_SUPPORTED when the multi-kernel decode path is in use. */
+int b200_engine_inject_withhold(b200_engine *e, int32_t cta);
+
 /* Raw handles for in-process callers (bench / tests): the engine's stream and
  * device status word. */
 void *b200_engine_stream(b200_engine *e);

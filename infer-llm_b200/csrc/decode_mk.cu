@@ -979,6 +979,7 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
     int cc = 0;
     const int64_t n_past = *p.n_past;
     const int32_t token = *p.token;
+    const int withheld = p.withhold ? *p.withhold - 1 : -1;  // test hook, normally -1
     bool ok = true;
     if (n_past < 0 || n_past >= p.n_ctx) {
         if (tid == 0) set_status(p.status, B200_DEV_BAD_POSITION);
@@ -1041,7 +1042,7 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
                 const float sg = gt / (1.0f + expf(-gt));
                 st_tagged(p.th + pr, up * sg, mine);
             }
-        } else {
+        } else if (!(ph == PH_QKV && l == 0 && b == withheld)) {
             u64 *dst = ph == PH_QKV ? p.tqkv : p.tx;
 #pragma unroll 1
             for (int64_t r = r0 + tid; r < r1; r += kCT) {

@@ -39,6 +39,10 @@ struct MkParams {
     unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
     int max_inflight = 16;             // ring copies outstanding per CTA (set by mk_launch)
     int split_keys = 32;               // keys per attention split (set by mk_launch)
+    // Failure injection for tests (device int, zero = none): CTA (*withhold - 1)
+    // does not publish its layer-0 QKV outputs, as if it had stopped, so the
+    // CTAs waiting for them run into their bounded waits.
+    const int32_t *withhold = nullptr;
 };
 
 // True if the megakernel supports this model shape on this device.

@@ -657,6 +657,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     const size_t o_tpo = take(2 * static_cast<int64_t>(mk_po_words(shape)));
     const size_t o_tpml = take(2 * static_cast<int64_t>(mk_pml_words(shape)));
     const size_t o_tao = take(2 * static_cast<int64_t>(e->Hq) * D);
+    const size_t o_withhold = take(64);
     const size_t o_mkl_n = take(64);
     e->act_bytes = off;
 
@@ -720,6 +721,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->mk.tpo = aw(o_tpo);
     e->mk.tpml = aw(o_tpml);
     e->mk.tao = aw(o_tao);
+    e->mk.withhold = ai(o_withhold);  // zeroed with the arena below: no injection
     e->mk.launches = reinterpret_cast<unsigned *>(e->act_arena + o_mkl_n);
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
@@ -941,6 +943,17 @@ int64_t b200_engine_n_past(const b200_engine *e) { return e ? e->n_past : -1; }
 int b200_engine_set_precision(b200_engine *e, int32_t precision) {
     if (!e || (precision != B200_PREC_FFMA && precision != B200_PREC_TF32)) return B200_ERR_INVALID_ARGUMENT;
     e->c.precision = precision;
+    return B200_OK;
+}
+
+int b200_engine_inject_withhold(b200_engine *e, int32_t cta) {
+    if (!e || !e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    if (!e->use_mk) return B200_ERR_NOT_SUPPORTED;
+    if (cta >= mk_grid()) return B200_ERR_OUT_OF_RANGE;
+    DeviceGuard dg(e->device);
+    const int32_t v = cta < 0 ? 0 : cta + 1;
+    B200_TRY(cudaMemcpyAsync(const_cast<int32_t *>(e->mk.withhold), &v, 4, cudaMemcpyHostToDevice, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
     return B200_OK;
 }
 

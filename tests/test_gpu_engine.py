@@ -127,6 +127,34 @@ def test_engine_errors_leave_state_unchanged(cuda, tiny):
     eng.close()
 
 
+def test_stopped_cta_is_reported_and_engine_recovers(cuda, tiny):
+    """Failure detection of the single-launch decode step without a GPU fault: one
+    CTA withholds its layer-0 QKV outputs (as if it had stopped), the CTAs waiting
+    for them give up after their bounded wait, the step reports B200_ERR_TIMEOUT and
+    commits nothing, and the same engine then reproduces the clean run."""
+    import time
+    cfg = G.QWEN3_TINY
+    eng = B.Engine(cfg, kv_capacity=64, max_batch=16, decode_mode=B.DECODE_SINGLE).load_gguf(tiny).finalize()
+    prompt = np.array([5, 17, 99, 3, 250, 8], np.int32)
+    clean = [eng.eval(prompt)] + [int(t) for t in eng.generate(4)]
+    eng.reset()
+    first = eng.eval(prompt)
+    assert first == clean[0]
+    lib = B.lib()
+    assert lib.b200_engine_inject_withhold(eng.h, 1) == 0
+    t0 = time.perf_counter()
+    with pytest.raises(B.B200Error) as e:
+        eng.generate(1)
+    assert e.value.status == 7  # B200_ERR_TIMEOUT
+    assert time.perf_counter() - t0 < 30.0
+    assert eng.n_past == len(prompt)  # nothing committed
+    assert lib.b200_engine_inject_withhold(eng.h, -1) == 0
+    eng.reset()
+    again = [eng.eval(prompt)] + [int(t) for t in eng.generate(4)]
+    assert again == clean
+    eng.close()
+
+
 def test_missing_weights_rejected(cuda):
     eng = B.Engine(G.QWEN3_TINY, kv_capacity=16, max_batch=4)
     with pytest.raises(B.B200Error):
