@@ -42,10 +42,38 @@ for _p in (os.path.join(REPO, "infer-llm_b200"), os.path.join(REPO, "oracle")):
 PROMPT_LEN = 32
 SEED = 0
 # DRAM bytes (read + write) of one decode_mk_kernel launch, from an ncu --set full
-# capture of `bench.py --steps 4 --warmup 3` (positions ~36; the per-step KV read
-# grows by 229,376 bytes per position, weights are 2,384,199,680 of it).
+# capture of `bench.py --steps 4 --warmup 3 --no-cpu-baseline` (positions ~36; the
+# per-step KV read grows by 229,376 bytes per position, weights are 2,384,199,680 of
+# it). TRAFFIC_SOURCE names the capture; the summary is under profiles/.
 TRAFFIC_PER_STEP = 2_395_436_000
+TRAFFIC_SOURCE = ("ncu --set full, one decode_mk_kernel launch of bench.py --steps 4 --warmup 3 "
+                  "(profiles/decode_mk_kernel_qwen3_0.6b_decode.md)")
 METRIC = "decode tok/s (Qwen3-0.6B-shape F32 bs1, 32-token prompt, greedy)"
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the CPU baseline record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def workload_config(model: str, plen: int, steps: int, world: int, tp: bool) -> dict:
+    """The `config` of a result line. Both arms (B200 and reference) report this same
+    dict for the same command line."""
+    cfg = model_cfg(model)
+    name = "0.6B" if model == "0.6b" else "8B"
+    return {"workload": f"Qwen3-{name} F32 decode, bs1, prompt {plen}, positions {plen}..{plen + steps - 1}",
+            "weights": f"seeded N(0,0.02) ({'GGUF' if model == '0.6b' else 'on-device Philox'}, seed {SEED})",
+            "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
+            "l2": f"inputs larger than L2 ({cfg.weight_bytes_per_token / 1e9:.2f} GB of weights "
+                  f"streamed per step{' over all ranks' if tp else ''})"}
 
 
 _OUT_FD = None  # the process's original stdout: the JSON result lines only
@@ -339,12 +367,7 @@ def run_b200(args):
         "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"Qwen3-{'0.6B' if args.model == '0.6b' else '8B'} F32 decode, bs1, prompt "
-                               f"{plen}, positions {plen}..{plen + steps - 1}",
-                   "weights": f"seeded N(0,0.02) ({'GGUF' if args.model == '0.6b' else 'on-device Philox'}, seed {SEED})",
-                   "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
-                   "l2": f"inputs larger than L2 ({cfg.weight_bytes_per_token / 1e9:.2f} GB of weights "
-                         f"streamed per step{' over all ranks' if tp else ''})"},
+        "config": workload_config(args.model, plen, steps, world, tp),
         "ttft_ms": round(float(np.median(ttft)), 3),
         "ttft_ms_tf32": round(float(np.median(ttft_tf32)), 3),
         "first_token_tf32_equal": bool(first_tf32 == first),
@@ -360,7 +383,8 @@ def run_b200(args):
         res["roofline"] = {"bound": "hbm", "kernel": "decode_mk_kernel (single-launch decode step)",
                            "achieved": round(step_gbs, 1), "peak": hbm, "unit": "GB/s",
                            "frac": round(step_gbs / hbm, 4), "peak_kind": peak_kind,
-                           "bytes_per_launch": step_b, "traffic": TRAFFIC_PER_STEP}
+                           "bytes_per_launch": step_b, "traffic": TRAFFIC_PER_STEP,
+                           "traffic_source": TRAFFIC_SOURCE}
     if ops:
         gb = gemv_bytes(cfg)
         gemv_us = sum(ops.get(k, 0.0) for k in gb)
@@ -382,13 +406,87 @@ def run_b200(args):
     if rank == 0 and world == 1 and args.model == "0.6b" and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_threads, sample_steps=args.cpu_sample_steps)
     res["first_tokens"] = [int(first)] + [int(t) for t in toks[:8]]
-    if tp:
-        eng.close()
-        dist.destroy_process_group()
-    elif world > 1:
+    eng.close()
+    if args.model == "0.6b" and not args.no_tp_8b:
+        # the model that shards: Qwen3-8B tensor-parallel over the same N GPUs (TP1 at N = 1)
+        res["tp_8b"] = tp_8b_block(world, rank, local, steps, warm)
+    if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         emit(res)
+
+
+def tp_8b_block(world, rank, local, steps, warm, plen=PROMPT_LEN):
+    """Qwen3-8B (BASELINE configs[4] shape, on-device seeded weights) decoded
+    tensor-parallel over the `world` ranks of this run (heads and FFN columns split,
+    one all-reduce after o_proj and after ffn_down, vocab-sharded greedy argmax):
+    tok/s of the one token stream, ms per token, the step's HBM roofline fraction over
+    the N ranks' combined peak, and the all-reduce share of the step (the 2 x n_layer
+    all-reduces of one token, timed back to back on the same GPUs with NCCL through
+    torch.distributed, over the measured ms per token)."""
+    import torch
+    import torch.distributed as dist
+
+    import b200infer as B
+    cfg = model_cfg("8b")
+    tp = world > 1
+    eng = B.Engine(cfg, kv_capacity=plen + steps + warm + 8, max_batch=plen, device=local,
+                   tp_rank=rank if tp else 0, tp_world=world)
+    eng.init_random(SEED)
+    if tp:
+        uid = [B.Engine.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.tp_init(uid[0])
+    eng.finalize()
+    stream = torch.cuda.ExternalStream(eng.stream())
+    prompt = prompt_ids(cfg, plen)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    eng.eval(prompt)
+    eng.generate(warm)
+    eng.reset()
+    barrier()
+    t0 = time.perf_counter()
+    eng.eval(prompt)
+    ttft = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    eng.generate(steps)
+    ev1.record(stream)
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / steps
+    launches = eng.decode_launches
+    eng.close()
+    hbm, peak_kind = peaks()
+    step_b = step_bytes(cfg, plen + steps // 2)
+    gbs = step_b / (ms * 1e-3) / 1e9
+    out = {"model": "Qwen3-8B F32", "parallelism": f"tp{world}", "prompt": plen, "steps": steps,
+           "value": round(1e3 / ms, 2), "unit": "tok/s", "ms_per_token": round(ms, 4), "ttft_ms": round(ttft, 3),
+           "roofline": {"bound": "hbm", "bytes_per_step": step_b, "achieved": round(gbs, 1),
+                        "peak": round(hbm * world, 1), "unit": "GB/s", "frac": round(gbs / (hbm * world), 4),
+                        "peak_kind": f"{peak_kind} x {world} ranks"},
+           "gpu_launches_per_token": launches}
+    if tp:
+        x = torch.zeros(cfg.n_embd, device=f"cuda:{local}")
+        n_ar = 2 * cfg.n_layer
+        for _ in range(10):
+            dist.all_reduce(x)
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(n_ar):
+            dist.all_reduce(x)
+        a1.record()
+        barrier()
+        ar_ms = max_over_ranks(a0.elapsed_time(a1), world)
+        out["allreduce"] = {"per_token": n_ar, "bytes_each": 4 * cfg.n_embd, "us_each_isolated": round(ar_ms * 1e3 / n_ar, 2),
+                            "share_of_step": round(ar_ms / ms, 4)}
+    return out
 
 
 def cpu_baseline(cfg, threads=0, sample_steps=16):
@@ -409,12 +507,39 @@ def cpu_baseline(cfg, threads=0, sample_steps=16):
     t2 = time.perf_counter()
     eng.close()
     return {"value": round(sample_steps / (t2 - t1), 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "cpu_model": cpu_model(), "nproc": os.cpu_count(),
             "ttft_ms": round((t1 - t0) * 1e3, 1),
             "sample": f"reference CPU backend, prompt {PROMPT_LEN} then {sample_steps} greedy decode tokens "
                       f"(INFERLLM_THREADS={threads})"}
 
 
+def _ref_replica(path, plen, steps, warm, threads, barrier, out):
+    """One reference CPU engine (spawned process): warm-up, then -- together with the
+    other replicas -- prefill + `steps` greedy tokens; puts (ttft s, decode s)."""
+    import oracle
+    from b200infer import gguf as G
+    cfg = model_cfg("0.6b")
+    eng = oracle.RefEngine(oracle.Ref(), path, threads=threads, capacity=plen + steps + warm + 8)
+    tok = eng.eval(prompt_ids(cfg, plen))
+    for _ in range(warm):
+        tok = eng.eval(np.array([tok], np.int32))
+    eng.reset()
+    barrier.wait()
+    t0 = time.perf_counter()
+    tok = eng.eval(prompt_ids(cfg, plen))
+    t1 = time.perf_counter()
+    for _ in range(steps):
+        tok = eng.eval(np.array([tok], np.int32))
+    t2 = time.perf_counter()
+    eng.close()
+    out.put((t1 - t0, t2 - t1))
+
+
 def run_reference(args):
+    """The reference CPU engine on this host's cores, same workload and config as the
+    B200 arm: one engine at N = 1; at N > 1 (torchrun) rank 0 runs N concurrent
+    replicas (spawned processes, cores / N threads each) as the B200 arm runs N
+    replicas, and value = all replicas' tokens / the slowest replica's time."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
@@ -428,34 +553,34 @@ def run_reference(args):
     if not oracle.Ref.available():
         emit({"impl": "reference", "unavailable": "oracle/_ref (reference built from source) missing"})
         return
-    threads = args.cpu_threads or (os.cpu_count() or 1)
-    ref = oracle.Ref()
+    cores = args.cpu_threads or (os.cpu_count() or 1)
+    threads = max(1, cores // world)
     path = G.cached_model(cfg, SEED)
     steps, warm, plen = args.steps, args.warmup, args.prompt
-    eng = oracle.RefEngine(ref, path, threads=threads, capacity=plen + steps + warm + 8)
-    tok = eng.eval(prompt_ids(cfg, plen))
-    for _ in range(warm):
-        tok = eng.eval(np.array([tok], np.int32))
-    eng.reset()
-    t0 = time.perf_counter()
-    tok = eng.eval(prompt_ids(cfg, plen))
-    ttft = time.perf_counter() - t0
-    t1 = time.perf_counter()
-    for _ in range(steps):
-        tok = eng.eval(np.array([tok], np.int32))
-    dt = time.perf_counter() - t1
-    eng.close()
-    value = steps / dt
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    barrier, out = ctx.Barrier(world), ctx.Queue()
+    procs = [ctx.Process(target=_ref_replica, args=(path, plen, steps, warm, threads, barrier, out))
+             for _ in range(world)]
+    for p in procs:
+        p.start()
+    res = [out.get(timeout=3600) for _ in procs]
+    for p in procs:
+        p.join()
+    ttft = max(r[0] for r in res)
+    dt = max(r[1] for r in res)
+    value = world * steps / dt
     emit({
-        "impl": "reference", "metric": METRIC.replace("32-token", f"{plen}-token"), "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC.replace("32-token", f"{plen}-token"), "value": round(value, 3),
+        "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"Qwen3-0.6B F32 decode, bs1, prompt {plen}, positions "
-                               f"{plen}..{plen + steps - 1}", "weights": f"seeded GGUF seed {SEED}",
-                   "parallelism": "single"},
+        "config": workload_config(args.model, plen, steps, world, False),
         "ttft_ms": round(ttft * 1e3, 1),
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{steps} greedy decode tokens after a {plen}-token prefill"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads * world, "kind": "reference",
+                         "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+                         "sample": f"{world} replica(s) x {threads} threads: {steps} greedy decode tokens after a "
+                                   f"{plen}-token prefill each"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
 
@@ -567,6 +692,8 @@ def main():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--cpu-sample-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-8b", action="store_true",
+                    help="skip the Qwen3-8B tensor-parallel block of the default (0.6B) run")
     ap.add_argument("--decode", choices=["auto", "multi", "single"], default="auto",
                     help="decode step: multi-kernel chain, single-launch kernel, or the engine's choice")
     args = ap.parse_args()

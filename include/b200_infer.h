@@ -159,9 +159,10 @@ size_t b200_argmax_workspace_bytes(int64_t n);
  * is a fixed library-owned device array of B200_ARGMAX_NOALLOC_SCRATCH bytes,
  * held by every GPU that loads the library until the process exits; the call
  * itself allocates nothing. Limits: n <= B200_ARGMAX_NOALLOC_MAX_N (larger n is
- * rejected with B200_ERR_INVALID_ARGUMENT). The first call on a device resolves
- * the array's device address (cudaGetSymbolAddress) and should come before any
- * stream capture on that device. All calls share the one array (the counter in it
+ * rejected with B200_ERR_INVALID_ARGUMENT). Every call looks up the array's device
+ * address (cudaGetSymbolAddress); the first call on a device also loads the
+ * library's device code there, so make it before any stream capture on that
+ * device. All calls share the one array (the counter in it
  * is cleared at the start of every call): calls that overlap on the GPU, on any
  * streams of the same device, race and must be serialised by the caller.
  * Results equal b200_argmax's. */
@@ -210,6 +211,18 @@ int b200_engine_memory(const b200_engine *e, size_t *weights, size_t *kv, size_t
  * only its rank's shard of the full tensor passed here. */
 int b200_engine_set_weight(b200_engine *e, const char *name, const float *host_data,
                            int64_t n_elements);
+/* Loads every tensor of a GGUF v3 file (F32 tensors named as above) into the
+ * weight arena: the file is memory-mapped and streamed through a pinned staging
+ * ring of `staging_bytes` (<= 0: 256 MiB) with asynchronous copies, and the call
+ * synchronizes once at the end. Every tensor is validated (name, size, type,
+ * bounds in the file) before the first copy. Replaces the reference's
+ * per-tensor synchronous upload (ModelBase::alloc_weight, model.cpp:562-572, and
+ * CUDABackend::copy_tensor_set, cuda_backend.cpp:106-112). */
+int b200_engine_load_gguf(b200_engine *e, const char *path, int64_t staging_bytes);
+/* Copies one weight tensor back to host memory in its GGUF shape (the inverse of
+ * b200_engine_set_weight; like CUDABackend::copy_tensor_get, cuda_backend.cpp).
+ * Single-GPU engines only (B200_ERR_NOT_SUPPORTED under tensor parallelism). */
+int b200_engine_get_weight(b200_engine *e, const char *name, float *host_out, int64_t n_elements);
 /* Fills every weight from the seeded generator of the given seed directly on the
  * device: matrices N(0, std), norm weights 1.0 (used when no GGUF is at hand). */
 int b200_engine_init_random(b200_engine *e, uint64_t seed, float std);
@@ -261,12 +274,21 @@ int b200_engine_profile_step(b200_engine *e, char *names, int name_len, float *u
 int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int max_kernels);
 
 /* Failure injection for tests of the single-launch decode step (no counterpart in
- * the reference): from the next decode step on, CTA `cta` of the step does not
- * publish its layer-0 QKV outputs, as if it had stopped; the CTAs waiting for them
- * give up after their bounded wait (2 s), the step returns B200_ERR_TIMEOUT and
- * commits nothing, and the engine stays usable. cta < 0 ends the injection.
- * B200_ERR_NOT_SUPPORTED when the multi-kernel decode path is in use. */
-int b200_engine_inject_withhold(b200_engine *e, int32_t cta);
+ * the reference): after `after_steps` more decode steps, CTA `cta` of every step
+ * does not publish its layer-0 QKV outputs, as if it had stopped; the CTAs waiting
+ * for them give up after their bounded wait (2 s), the call returns
+ * B200_ERR_TIMEOUT and commits nothing (eval and generate leave n_past and the
+ * next input token as before the call), and the engine stays usable without a
+ * reset. cta < 0 ends the injection. B200_ERR_NOT_SUPPORTED when the multi-kernel
+ * decode path is in use. */
+int b200_engine_inject_withhold(b200_engine *e, int32_t cta, int32_t after_steps);
+
+/* Test hook of the single-launch decode step (no counterpart in the reference):
+ * sets its launch counter as if `launches` steps had run, so a test can take the
+ * step's exchange tags across their wrap-around (every 2^24 - 1 launches) without
+ * running millions of steps. Results must not change. B200_ERR_NOT_SUPPORTED when
+ * the multi-kernel decode path is in use. */
+int b200_engine_set_decode_launch_counter(b200_engine *e, uint64_t launches);
 
 /* Raw handles for in-process callers (bench / tests): the engine's stream and
  * device status word. */

@@ -65,11 +65,25 @@ class Engine:
         _chk("b200_engine_set_weight " + name,
              lib().b200_engine_set_weight(self.h, name.encode(), C.c_void_p(arr.ctypes.data), arr.size))
 
-    def load_gguf(self, path: str):
+    def load_gguf(self, path: str, staging_bytes: int = 0):
+        """All tensors of a GGUF file through the native loader (memory-mapped,
+        pinned staging ring, asynchronous copies, one synchronization)."""
+        _chk("b200_engine_load_gguf", lib().b200_engine_load_gguf(self.h, path.encode(), staging_bytes))
+        return self
+
+    def load_gguf_per_tensor(self, path: str):
+        """The same file one synchronous set_weight per tensor (the reference's upload shape)."""
         rd = GGUFReader(path)
         for name in rd.names():
             self.set_weight(name, rd.tensor(name))
         return self
+
+    def get_weight(self, name: str, shape) -> np.ndarray:
+        """One weight back from the device in its GGUF (numpy) shape; single GPU only."""
+        out = np.empty(shape, np.float32)
+        _chk("b200_engine_get_weight " + name,
+             lib().b200_engine_get_weight(self.h, name.encode(), C.c_void_p(out.ctypes.data), out.size))
+        return out
 
     def init_random(self, seed: int, std: float = 0.02):
         _chk("b200_engine_init_random", lib().b200_engine_init_random(self.h, seed, std))

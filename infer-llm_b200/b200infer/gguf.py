@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import os
 import struct
+import tempfile
 import zlib
 from dataclasses import dataclass, asdict
 
@@ -254,10 +255,14 @@ class GGUFReader:
 
 def cached_model(cfg: Qwen3Config, seed: int, directory: str | None = None) -> str:
     """Path of the seeded GGUF for (cfg, seed), writing it once if absent."""
-    directory = directory or os.environ.get("B200_MODEL_DIR", "/tmp/b200_models")
+    directory = directory or os.environ.get("B200_MODEL_DIR",
+                                            os.path.join(tempfile.gettempdir(), "b200_models"))
     os.makedirs(directory, exist_ok=True)
     key = zlib.crc32(repr(sorted(cfg.as_dict().items())).encode())
     path = os.path.join(directory, f"b200_qwen3_{cfg.n_layer}L{cfg.n_embd}_{key:08x}_s{seed}.gguf")
     if not os.path.exists(path):
-        write_gguf(path, cfg, seed)
+        # written under a private name and renamed: a reader never sees a partial file
+        tmp = f"{path}.{os.getpid()}.part"
+        write_gguf(tmp, cfg, seed)
+        os.replace(tmp, path)
     return path

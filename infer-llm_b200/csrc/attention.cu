@@ -714,15 +714,16 @@ cudaError_t dec_launch(const AttnArgs &a, int S, cudaStream_t stream, bool pdl) 
     const size_t smem =
         (4 * kDecTile * (D + 4) + G * D + 2 * D + G * kDecTile + G + 2 * G + G * D) * sizeof(float);
     auto kern = attn_decode_kernel<D, G>;
-    static bool configured = false;  // one instance per template instantiation
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     cudaSharedmemCarveoutMaxShared);
+    {
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(kern), ATTR_SMEM, [&] {
+            cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (r == cudaSuccess) r = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
+            return r;
+        });
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, static_cast<unsigned>(a.Hkv));
@@ -754,11 +755,11 @@ template <int D, int G>
 cudaError_t d2_launch(const AttnArgs &a, int S, cudaStream_t stream, bool pdl) {
     const size_t smem = d2_smem_bytes<D, G>();
     auto kern = attn_decode_tma_kernel<D, G>;
-    static bool configured = false;  // one instance per template instantiation
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    {
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(kern), ATTR_SMEM, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        });
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     // positions the maps cover: the cache capacity (engine) or the keys of this call
     const int64_t rows = a.kv_rows > 0 ? a.kv_rows : a.n_past + 1;
@@ -773,11 +774,11 @@ cudaError_t pre_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
     constexpr int BQ = kRows / G;
     const size_t smem = ((kRows + 2 * kKeys) * (D + 4) + kRows * (kKeys + 4)) * sizeof(float);
     auto kern = attn_prefill_kernel<D, G>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    {
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(kern), ATTR_SMEM, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        });
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     const dim3 grid(static_cast<unsigned>((a.Tq + BQ - 1) / BQ), static_cast<unsigned>(a.Hkv));
     return b200_launch(kern, grid, dim3(kPreThreads), smem, stream, pdl, a);

@@ -5,6 +5,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <tuple>
+
 #include "../../include/b200_infer.h"
 
 #define B200_HOST_DEVICE __host__ __device__ __forceinline__
@@ -266,19 +270,38 @@ B200_DEVICE float rms_scale_from_sumsq(double sumsq, int64_t D, float eps) {
 
 }  // namespace b200
 
+namespace b200 {
+// Kernel function attributes (cudaFuncSetAttribute) belong to the current device:
+// `set()` runs once per (device, kernel, attribute group) and is recorded only when
+// it succeeded, so a second GPU driven from the same process configures its own.
+template <typename Set>
+inline cudaError_t once_per_device(const void *kernel, int what, Set set) {
+    static std::mutex mu;
+    static std::set<std::tuple<int, const void *, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const auto key = std::make_tuple(dev, kernel, what);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count(key)) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess) done.insert(key);
+    return e;
+}
+enum { ATTR_CARVEOUT = 0, ATTR_SMEM = 1 };
+}  // namespace b200
+
 // Host-side launch helper: launch with the PDL attribute on `stream`.
 // Every kernel asks for the maximum shared-memory carveout, so consecutive kernels
 // never need an SM reconfiguration (which would serialise programmatic launches).
 template <typename Kernel, typename... Args>
 static inline cudaError_t b200_launch(Kernel kernel, dim3 grid, dim3 block, size_t smem,
                                       cudaStream_t stream, bool pdl, Args... args) {
-    static bool carveout_set = false;  // one instance per kernel type
-    if (!carveout_set) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                             cudaSharedmemCarveoutMaxShared);
-        if (e != cudaSuccess) return e;
-        carveout_set = true;
-    }
+    cudaError_t e = b200::once_per_device(reinterpret_cast<const void *>(kernel), b200::ATTR_CARVEOUT, [&] {
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared);
+    });
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

@@ -208,12 +208,14 @@ B200_DEVICE bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int32_t *stat
 // Tagged activation words. Every value one CTA hands to others is stored as one
 // 64-bit word (tag << 32 | float bits) with a single relaxed gpu-scope store, so
 // a reader that sees the tag it expects also sees the value of that phase: no
-// fence, no flag, no grid barrier. Tags are (launch + 1) * kTagStride + phase
-// index, unique per launch (the launch counter advances on every launch, aborted
-// ones included), so nothing left over from an earlier step ever matches.
+// fence, no flag, no grid barrier. Tags are (launch mod kMkTagPeriod + 1) *
+// kTagStride + phase index (the launch counter advances on every launch, aborted
+// ones included, and the host clears it with the words before a period can pass),
+// so nothing left over from an earlier step ever matches.
 // A buffer is rewritten only two phases after it was read, and every phase needs
 // the previous phase's outputs of all CTAs, so no writer can overtake a reader.
 constexpr uint32_t kTagStride = 256;  // > 5 * kMaxLayers + 1 phase indices
+static_assert((kMkTagPeriod + 1) * kTagStride <= (1ull << 32), "tags fit 32 bits");
 using u64 = unsigned long long;
 
 B200_DEVICE uint32_t tag_hi(u64 w) { return static_cast<uint32_t>(w >> 32); }
@@ -945,8 +947,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
     const int b = blockIdx.x, G = gridDim.x;
     if (tid == 0) {
         // every CTA of every launch takes one ticket: launch = ticket / G
-        const unsigned ticket = atomicAdd(p.launches, 1u);
-        s_tag0 = (ticket / static_cast<unsigned>(G) + 1u) * kTagStride;
+        const unsigned long long ticket = atomicAdd(p.launches, 1ull);
+        const unsigned long long launch = ticket / static_cast<unsigned long long>(G);
+        s_tag0 = static_cast<uint32_t>(launch % kMkTagPeriod + 1ull) * kTagStride;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);  // the one warp that reads the slot's chunk
@@ -979,7 +982,20 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
     int cc = 0;
     const int64_t n_past = *p.n_past;
     const int32_t token = *p.token;
-    const int withheld = p.withhold ? *p.withhold - 1 : -1;  // test hook, normally -1
+    // test hook, normally -1: CTA withhold[0] - 1 withholds its layer-0 QKV outputs
+    // once withhold[1] more launches have passed (that CTA counts them down)
+    __shared__ int s_withheld;
+    if (tid == 0) {
+        int w = -1;
+        if (p.withhold && p.withhold[0] - 1 == b) {
+            const int skip = p.withhold[1];
+            if (skip > 0)
+                p.withhold[1] = skip - 1;
+            else
+                w = b;
+        }
+        s_withheld = w;
+    }
     bool ok = true;
     if (n_past < 0 || n_past >= p.n_ctx) {
         if (tid == 0) set_status(p.status, B200_DEV_BAD_POSITION);
@@ -1000,6 +1016,7 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
     }
     mk.rope_table(ok ? n_past : 0);
     named_sync(1, kCT);
+    const int withheld = s_withheld;
     // One pass over the step's phases (per layer QKV, attention, o_proj, gate/up,
     // down; then the LM head), each helper called from exactly one place so that
     // the kernel's code stays small enough for the instruction cache.

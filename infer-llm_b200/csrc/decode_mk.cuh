@@ -26,7 +26,12 @@ struct MkParams {
     unsigned long long *tpo = nullptr;   // attention split partial outputs [max_splits][Hq][D]
     unsigned long long *tpml = nullptr;  // attention split (max, sum) [max_splits][Hq][2]
     unsigned long long *tao = nullptr;   // merged attention output [Hq][D]
-    unsigned *launches = nullptr;        // + gridDim.x per launch: the tag base (zero at create)
+    // Tickets: every CTA of every launch takes one (64-bit: never wraps), launch =
+    // ticket / gridDim.x; the tag base is derived from the launch modulo
+    // kMkTagPeriod. The engine clears this counter together with the tagged words
+    // above before kMkClearEvery launches have run since the last clear, so no word
+    // can be as old as one tag period.
+    unsigned long long *launches = nullptr;
     float *logits = nullptr;           // [V] or nullptr
     int32_t *token = nullptr;          // in: token of this step; out: greedy next token
     int32_t *n_past = nullptr;         // advanced by 1 at the end of the step
@@ -39,11 +44,17 @@ struct MkParams {
     unsigned long long *trace = nullptr;  // optional: [5 n_layer + 1] x 8 words (phase stamps)
     int max_inflight = 16;             // ring copies outstanding per CTA (set by mk_launch)
     int split_keys = 32;               // keys per attention split (set by mk_launch)
-    // Failure injection for tests (device int, zero = none): CTA (*withhold - 1)
-    // does not publish its layer-0 QKV outputs, as if it had stopped, so the
-    // CTAs waiting for them run into their bounded waits.
-    const int32_t *withhold = nullptr;
+    // Failure injection for tests (two device ints, zero = none): CTA
+    // (withhold[0] - 1) does not publish its layer-0 QKV outputs, as if it had
+    // stopped, so the CTAs waiting for them run into their bounded waits; it lets
+    // withhold[1] launches pass first (counting them down).
+    int32_t *withhold = nullptr;
 };
+
+// Tags are (launch mod kMkTagPeriod + 1) * 256 + phase: 32-bit, never 0 (cleared
+// words never match). Launches between two clears stay below kMkClearEvery.
+constexpr unsigned long long kMkTagPeriod = (1ull << 24) - 1;
+constexpr long long kMkClearEvery = 1ll << 23;
 
 // True if the megakernel supports this model shape on this device.
 bool mk_supported(const MkParams &p);

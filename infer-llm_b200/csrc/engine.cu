@@ -16,6 +16,12 @@
 // host round trip (under tensor parallelism with the NCCL all-reduces and the
 // token all-gather inside the graph). Prefill uses the tiled FFMA / tcgen05 GEMMs and the tiled
 // attention kernel over all prompt rows and samples from the last row only.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -140,6 +146,11 @@ struct b200_engine {
     bool use_mk = false;
     MkParams mk;
     MkLayer *mk_layers = nullptr;  // device table
+    // the step's tagged exchange words (one contiguous range of the activation
+    // arena), cleared with the launch counter before kMkClearEvery launches have run
+    unsigned char *mk_words = nullptr;
+    size_t mk_words_bytes = 0;
+    long long mk_since_clear = 0;
 };
 
 namespace {
@@ -523,6 +534,14 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
     return B200_OK;
 }
 
+// Device n_past := the host's committed n_past (after a failed step).
+int restore_n_past(b200_engine *e) {
+    e->pinned_io[e->io_tok + 3] = static_cast<int32_t>(e->n_past);
+    B200_TRY(cudaMemcpyAsync(e->n_past_dev, e->pinned_io + e->io_tok + 3, 4, cudaMemcpyHostToDevice, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    return B200_OK;
+}
+
 int check_status(b200_engine *e) {
     int32_t s = 0;
     B200_TRY(cudaMemcpyAsync(&s, e->status, 4, cudaMemcpyDeviceToHost, e->stream));
@@ -537,6 +556,22 @@ int check_status(b200_engine *e) {
     if (s == B200_DEV_TIMEOUT) return B200_ERR_TIMEOUT;
     if (s == B200_DEV_BAD_TOKEN || s == B200_DEV_BAD_POSITION) return B200_ERR_OUT_OF_RANGE;
     return B200_ERR_DEVICE_CHECK;
+}
+
+// Accounts for n single-launch decode steps about to be enqueued on the engine
+// stream. Tags repeat after kMkTagPeriod launches; before kMkClearEvery launches
+// have run since the last clear, the tagged words and the launch counter are
+// cleared together (stream-ordered, before the launches), so no word left by an
+// earlier launch can carry a tag of a later one.
+int mk_account(b200_engine *e, int64_t n) {
+    if (!e->use_mk || n <= 0) return B200_OK;
+    if (e->mk_since_clear + n > kMkClearEvery) {
+        B200_TRY(cudaMemsetAsync(e->mk_words, 0, e->mk_words_bytes, e->stream));
+        B200_TRY(cudaMemsetAsync(e->mk.launches, 0, 8, e->stream));
+        e->mk_since_clear = 0;
+    }
+    e->mk_since_clear += n;
+    return B200_OK;
 }
 
 int build_graph(b200_engine *e) {
@@ -722,7 +757,9 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->mk.tpml = aw(o_tpml);
     e->mk.tao = aw(o_tao);
     e->mk.withhold = ai(o_withhold);  // zeroed with the arena below: no injection
-    e->mk.launches = reinterpret_cast<unsigned *>(e->act_arena + o_mkl_n);
+    e->mk.launches = reinterpret_cast<unsigned long long *>(e->act_arena + o_mkl_n);
+    e->mk_words = e->act_arena + o_tx;
+    e->mk_words_bytes = o_withhold - o_tx;  // the tagged words (tx .. tao)
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
     std::vector<float> hf(D / 2);
@@ -768,78 +805,296 @@ int b200_engine_memory(const b200_engine *e, size_t *weights, size_t *kv, size_t
     return B200_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Where one GGUF tensor lives in the engine's weight arena: `rows` rows of `width`
+// floats, taken from the host tensor at src_off + row * spitch (floats) and stored
+// at dst + row * dpitch. Every weight is one such block: whole tensors, this rank's
+// row or column shard, the q / k / v rows of the fused QKV matrix, the interleaved
+// gate / up rows.
+struct WeightBlock {
+    float *dst = nullptr;
+    int64_t dpitch = 0, src_off = 0, spitch = 0, width = 0, rows = 0;
+};
+
+// The block of tensor `name` (n elements in its GGUF shape); B200_ERR_INVALID_ARGUMENT
+// for an unknown name or a wrong size.
+int weight_block(b200_engine *e, const std::string &nm, int64_t n, WeightBlock *out) {
+    const b200_qwen3_config &c = e->c;
+    const int64_t r = c.tp_rank;
+    const int64_t H = e->H, D = e->D, F = e->F, V = e->V;
+    const int64_t Hq_all = c.n_head, Hkv_all = c.n_head_kv;
+    auto whole = [&](float *dst, int64_t floats) {  // a vector: one row
+        *out = WeightBlock{dst, floats, 0, floats, floats, 1};
+        return B200_OK;
+    };
+    // rows [row0, row0 + rows) of a [N][K] matrix, into dst with pitch dpitch
+    auto rows_of = [&](float *dst, int64_t dpitch, int64_t K, int64_t row0, int64_t rows) {
+        *out = WeightBlock{dst, dpitch, row0 * K, K, K, rows};
+        return B200_OK;
+    };
+    int layer = -1;
+    const char *rest = nullptr;
+    if (nm == "token_embd.weight") {  // full on every rank (the gather needs any row)
+        if (n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
+        return rows_of(e->tok_embd, H, H, 0, c.n_vocab);
+    }
+    if (nm == "output_norm.weight") return n == H ? whole(e->out_norm, H) : B200_ERR_INVALID_ARGUMENT;
+    if (nm == "output.weight") {
+        if (c.tied || n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
+        return rows_of(e->lm_head, H, H, e->vocab_off, V);  // this rank's vocabulary rows
+    }
+    if (!parse_layer(nm.c_str(), &layer, &rest) || layer < 0 || layer >= c.n_layer) return B200_ERR_INVALID_ARGUMENT;
+    LayerW &w = e->L[layer];
+    const std::string p(rest);
+    if (p == "attn_norm.weight" || p == "ffn_norm.weight")
+        return n == H ? whole(p[0] == 'a' ? w.attn_norm : w.ffn_norm, H) : B200_ERR_INVALID_ARGUMENT;
+    if (p == "attn_q_norm.weight" || p == "attn_k_norm.weight")
+        return n == D ? whole(p[5] == 'q' ? w.q_norm : w.k_norm, D) : B200_ERR_INVALID_ARGUMENT;
+    if (p == "attn_q.weight") {
+        if (n != Hq_all * D * H) return B200_ERR_INVALID_ARGUMENT;
+        return rows_of(w.wqkv, H, H, r * e->Hq * D, e->Hq * D);
+    }
+    if (p == "attn_k.weight" || p == "attn_v.weight") {
+        if (n != Hkv_all * D * H) return B200_ERR_INVALID_ARGUMENT;
+        float *dst = w.wqkv + (e->Hq + (p[5] == 'k' ? 0 : e->Hkv)) * D * H;
+        return rows_of(dst, H, H, r * e->Hkv * D, e->Hkv * D);
+    }
+    if (p == "attn_output.weight") {
+        // [H][Hq*D]: this rank's column block (row-split for tensor parallelism)
+        if (n != H * Hq_all * D) return B200_ERR_INVALID_ARGUMENT;
+        const int64_t kc = e->Hq * D;
+        *out = WeightBlock{w.wo, kc, r * kc, Hq_all * D, kc, H};
+        return B200_OK;
+    }
+    if (p == "ffn_gate.weight" || p == "ffn_up.weight") {
+        // interleaved: packed row 2i = gate row i, 2i+1 = up row i
+        if (n != static_cast<int64_t>(c.n_ff) * H) return B200_ERR_INVALID_ARGUMENT;
+        *out = WeightBlock{w.wgu + (p[4] == 'g' ? 0 : H), 2 * H, r * F * H, H, H, F};
+        return B200_OK;
+    }
+    if (p == "ffn_down.weight") {
+        if (n != H * static_cast<int64_t>(c.n_ff)) return B200_ERR_INVALID_ARGUMENT;
+        *out = WeightBlock{w.wdown, F, r * F, static_cast<int64_t>(c.n_ff), F, H};
+        return B200_OK;
+    }
+    return B200_ERR_INVALID_ARGUMENT;
+}
+
+// Rows [a, b) of a block between the host tensor and the arena (one 2-D copy).
+cudaError_t copy_rows(const WeightBlock &wb, float *host, int64_t a, int64_t b, cudaMemcpyKind kind, cudaStream_t st) {
+    float *dev = wb.dst + a * wb.dpitch;
+    float *hst = host + wb.src_off + a * wb.spitch;
+    if (kind == cudaMemcpyHostToDevice)
+        return cudaMemcpy2DAsync(dev, wb.dpitch * 4, hst, wb.spitch * 4, wb.width * 4, b - a, kind, st);
+    return cudaMemcpy2DAsync(hst, wb.spitch * 4, dev, wb.dpitch * 4, wb.width * 4, b - a, kind, st);
+}
+
+void mark_loaded(b200_engine *e, const std::string &nm) {
+    for (size_t i = 0; i < e->missing.size(); ++i)
+        if (e->missing[i] == nm) {
+            e->missing.erase(e->missing.begin() + i);
+            return;
+        }
+}
+
+// ---- minimal GGUF v3 reader (gguf_parser.cpp:100-125 reads the same layout):
+// header, metadata records (skipped except general.alignment), tensor infos.
+struct GgufTensor {
+    std::string name;
+    int64_t n = 0;
+    uint32_t type = 0;
+    uint64_t offset = 0;
+};
+
+struct GgufFile {
+    const unsigned char *base = nullptr;
+    size_t size = 0, pos = 0;
+    bool ok = true;
+    template <class T> T get() {
+        T v{};
+        if (pos + sizeof(T) > size) {
+            ok = false;
+            return v;
+        }
+        std::memcpy(&v, base + pos, sizeof(T));
+        pos += sizeof(T);
+        return v;
+    }
+    std::string str() {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || n > size - pos) {
+            ok = false;
+            return {};
+        }
+        std::string s(reinterpret_cast<const char *>(base + pos), n);
+        pos += n;
+        return s;
+    }
+    // skips one metadata value of GGUF type t
+    void skip(uint32_t t, int depth = 0) {
+        static const size_t fixed[] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+        if (t == 8) {
+            str();
+        } else if (t == 9) {
+            const uint32_t et = get<uint32_t>();
+            const uint64_t cnt = get<uint64_t>();
+            if (!ok || depth > 2) {
+                ok = false;
+                return;
+            }
+            if (et != 8 && et != 9 && et < 13) {
+                if (cnt > (size - pos) / fixed[et]) {
+                    ok = false;
+                    return;
+                }
+                pos += cnt * fixed[et];
+            } else {
+                for (uint64_t i = 0; i < cnt && ok; ++i) skip(et, depth + 1);
+            }
+        } else if (t < 13) {
+            if (fixed[t] > size - pos) {
+                ok = false;
+                return;
+            }
+            pos += fixed[t];
+        } else {
+            ok = false;
+        }
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
 int b200_engine_set_weight(b200_engine *e, const char *name, const float *host, int64_t n) {
     if (!e || !name || !host) return B200_ERR_INVALID_ARGUMENT;
     if (e->finalized) return B200_ERR_INVALID_ARGUMENT;
     DeviceGuard dg(e->device);
-    const b200_qwen3_config &c = e->c;
-    const int r = c.tp_rank;
-    const int64_t H = e->H, D = e->D, F = e->F, V = e->V;
-    const int64_t Hq_all = c.n_head, Hkv_all = c.n_head_kv;
-    cudaStream_t st = e->stream;
-    auto h2d = [&](float *dst, const float *src, int64_t floats) {
-        return cudaMemcpyAsync(dst, src, floats * 4, cudaMemcpyHostToDevice, st);
-    };
-    // rows [row0, row0+rows) of a [N][K] host matrix into dst with pitch dpitch floats
-    auto rows2d = [&](float *dst, int64_t dpitch, const float *src, int64_t K, int64_t row0, int64_t rows) {
-        return cudaMemcpy2DAsync(dst, dpitch * 4, src + row0 * K, K * 4, K * 4, rows, cudaMemcpyHostToDevice, st);
-    };
-    cudaError_t err = cudaSuccess;
-    std::string nm(name);
-    int layer = -1;
-    const char *rest = nullptr;
-    if (nm == "token_embd.weight") {
-        if (n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
-        err = h2d(e->tok_embd, host, n);
-    } else if (nm == "output_norm.weight") {
-        if (n != H) return B200_ERR_INVALID_ARGUMENT;
-        err = h2d(e->out_norm, host, n);
-    } else if (nm == "output.weight") {
-        if (c.tied || n != static_cast<int64_t>(c.n_vocab) * H) return B200_ERR_INVALID_ARGUMENT;
-        err = h2d(e->lm_head, host + e->vocab_off * H, V * H);
-    } else if (parse_layer(name, &layer, &rest) && layer >= 0 && layer < c.n_layer) {
-        LayerW &w = e->L[layer];
-        const std::string p(rest);
-        if (p == "attn_norm.weight" || p == "ffn_norm.weight") {
-            if (n != H) return B200_ERR_INVALID_ARGUMENT;
-            err = h2d(p[0] == 'a' ? w.attn_norm : w.ffn_norm, host, H);
-        } else if (p == "attn_q_norm.weight" || p == "attn_k_norm.weight") {
-            if (n != D) return B200_ERR_INVALID_ARGUMENT;
-            err = h2d(p[5] == 'q' ? w.q_norm : w.k_norm, host, D);
-        } else if (p == "attn_q.weight") {
-            if (n != Hq_all * D * H) return B200_ERR_INVALID_ARGUMENT;
-            err = rows2d(w.wqkv, H, host, H, r * e->Hq * D, e->Hq * D);
-        } else if (p == "attn_k.weight" || p == "attn_v.weight") {
-            if (n != Hkv_all * D * H) return B200_ERR_INVALID_ARGUMENT;
-            float *dst = w.wqkv + (e->Hq + (p[5] == 'k' ? 0 : e->Hkv)) * D * H;
-            err = rows2d(dst, H, host, H, r * e->Hkv * D, e->Hkv * D);
-        } else if (p == "attn_output.weight") {
-            // [H][Hq*D]: keep this rank's column block (row-split for tensor parallelism)
-            if (n != H * Hq_all * D) return B200_ERR_INVALID_ARGUMENT;
-            const int64_t kc = e->Hq * D;
-            err = cudaMemcpy2DAsync(w.wo, kc * 4, host + r * kc, Hq_all * D * 4, kc * 4, H, cudaMemcpyHostToDevice, st);
-        } else if (p == "ffn_gate.weight" || p == "ffn_up.weight") {
-            // interleave: packed row 2i = gate row i, 2i+1 = up row i
-            if (n != static_cast<int64_t>(c.n_ff) * H) return B200_ERR_INVALID_ARGUMENT;
-            float *dst = w.wgu + (p[4] == 'g' ? 0 : H);
-            err = cudaMemcpy2DAsync(dst, 2 * H * 4, host + r * F * H, H * 4, H * 4, F, cudaMemcpyHostToDevice, st);
-        } else if (p == "ffn_down.weight") {
-            if (n != H * static_cast<int64_t>(c.n_ff)) return B200_ERR_INVALID_ARGUMENT;
-            err = cudaMemcpy2DAsync(w.wdown, F * 4, host + r * F, static_cast<int64_t>(c.n_ff) * 4, F * 4, H,
-                                    cudaMemcpyHostToDevice, st);
-        } else {
-            return B200_ERR_INVALID_ARGUMENT;
-        }
-    } else {
+    WeightBlock wb;
+    const int rc = weight_block(e, name, n, &wb);
+    if (rc != B200_OK) return rc;
+    cudaError_t err = copy_rows(wb, const_cast<float *>(host), 0, wb.rows, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);  // host buffer may be released after return
+    if (err != cudaSuccess) return from_cuda(err);
+    mark_loaded(e, name);
+    return B200_OK;
+}
+
+int b200_engine_get_weight(b200_engine *e, const char *name, float *host_out, int64_t n) {
+    if (!e || !name || !host_out) return B200_ERR_INVALID_ARGUMENT;
+    if (e->c.tp_world != 1) return B200_ERR_NOT_SUPPORTED;
+    DeviceGuard dg(e->device);
+    WeightBlock wb;
+    const int rc = weight_block(e, name, n, &wb);
+    if (rc != B200_OK) return rc;
+    cudaError_t err = copy_rows(wb, host_out, 0, wb.rows, cudaMemcpyDeviceToHost, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    return from_cuda(err);
+}
+
+int b200_engine_load_gguf(b200_engine *e, const char *path, int64_t staging_bytes) {
+    if (!e || !path || e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    if (staging_bytes <= 0) staging_bytes = int64_t(256) << 20;
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return B200_ERR_INVALID_ARGUMENT;
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size < 24) {
+        close(fd);
         return B200_ERR_INVALID_ARGUMENT;
     }
-    if (err == cudaSuccess) err = cudaStreamSynchronize(st);  // host buffer may be released after return
-    if (err != cudaSuccess) return from_cuda(err);
-    for (size_t i = 0; i < e->missing.size(); ++i)
-        if (e->missing[i] == nm) {
-            e->missing.erase(e->missing.begin() + i);
+    const size_t fsize = static_cast<size_t>(sb.st_size);
+    void *map = mmap(nullptr, fsize, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return B200_ERR_INVALID_ARGUMENT;
+    madvise(map, fsize, MADV_SEQUENTIAL);
+    GgufFile g{static_cast<const unsigned char *>(map), fsize};
+    int rc = B200_OK;
+    std::vector<GgufTensor> ts;
+    uint64_t align = 32;
+    if (g.get<uint32_t>() != 0x46554747u || g.get<uint32_t>() != 3u) rc = B200_ERR_INVALID_ARGUMENT;
+    const uint64_t n_tensors = g.get<uint64_t>(), n_kv = g.get<uint64_t>();
+    for (uint64_t i = 0; rc == B200_OK && g.ok && i < n_kv; ++i) {
+        const std::string key = g.str();
+        const uint32_t t = g.get<uint32_t>();
+        if (key == "general.alignment" && t == 4) {
+            align = g.get<uint32_t>();
+            if (align == 0 || (align & (align - 1))) rc = B200_ERR_INVALID_ARGUMENT;
+        } else {
+            g.skip(t);
+        }
+    }
+    for (uint64_t i = 0; rc == B200_OK && g.ok && i < n_tensors; ++i) {
+        GgufTensor t;
+        t.name = g.str();
+        const uint32_t nd = g.get<uint32_t>();
+        t.n = 1;
+        for (uint32_t d = 0; d < nd && d < 4; ++d) t.n *= static_cast<int64_t>(g.get<uint64_t>());
+        if (nd > 4) rc = B200_ERR_INVALID_ARGUMENT;
+        t.type = g.get<uint32_t>();
+        t.offset = g.get<uint64_t>();
+        ts.push_back(std::move(t));
+    }
+    if (!g.ok) rc = B200_ERR_INVALID_ARGUMENT;
+    const size_t data0 = (g.pos + align - 1) / align * align;
+    // validate every tensor before the first copy
+    std::vector<WeightBlock> blocks(ts.size());
+    for (size_t i = 0; rc == B200_OK && i < ts.size(); ++i) {
+        const GgufTensor &t = ts[i];
+        if (t.type != 0 /* F32 */ || t.n <= 0 || t.offset > fsize || data0 + t.offset + 4 * static_cast<uint64_t>(t.n) > fsize)
+            rc = B200_ERR_INVALID_ARGUMENT;
+        else
+            rc = weight_block(e, t.name, t.n, &blocks[i]);
+    }
+    DeviceGuard dg(e->device);
+    // Pinned staging ring: the host copies row blocks of the mapping into a slot
+    // while the copy engine drains the previous slots; a slot is reused once the
+    // event recorded after its last copy has completed. One sync at the end.
+    constexpr int kSlots = 4;
+    const size_t slot_bytes = std::max<size_t>(static_cast<size_t>(staging_bytes) / kSlots, size_t(1) << 20);
+    unsigned char *pinned = nullptr;
+    cudaEvent_t ev[kSlots] = {};
+    bool used[kSlots] = {};
+    cudaError_t err = cudaSuccess;
+    if (rc == B200_OK) err = cudaMallocHost(&pinned, slot_bytes * kSlots);
+    for (int i = 0; err == cudaSuccess && i < kSlots; ++i) err = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+    int slot = 0;
+    for (size_t i = 0; rc == B200_OK && err == cudaSuccess && i < ts.size(); ++i) {
+        const WeightBlock &wb = blocks[i];
+        const float *src = reinterpret_cast<const float *>(g.base + data0 + ts[i].offset);
+        const int64_t row_bytes = wb.width * 4;
+        if (row_bytes > static_cast<int64_t>(slot_bytes)) {
+            rc = B200_ERR_INVALID_ARGUMENT;  // a single row larger than a slot
             break;
         }
+        const int64_t rows_per_slot = static_cast<int64_t>(slot_bytes) / row_bytes;
+        for (int64_t a = 0; a < wb.rows && err == cudaSuccess; a += rows_per_slot) {
+            const int64_t b = std::min(wb.rows, a + rows_per_slot);
+            if (used[slot]) err = cudaEventSynchronize(ev[slot]);
+            if (err != cudaSuccess) break;
+            float *stage = reinterpret_cast<float *>(pinned + slot * slot_bytes);
+            for (int64_t row = a; row < b; ++row)
+                std::memcpy(stage + (row - a) * wb.width, src + wb.src_off + row * wb.spitch, row_bytes);
+            // the staged rows are packed: source pitch = width
+            err = cudaMemcpy2DAsync(wb.dst + a * wb.dpitch, wb.dpitch * 4, stage, row_bytes, row_bytes, b - a,
+                                    cudaMemcpyHostToDevice, e->stream);
+            if (err == cudaSuccess) err = cudaEventRecord(ev[slot], e->stream);
+            used[slot] = true;
+            slot = (slot + 1) % kSlots;
+        }
+    }
+    const cudaError_t serr = cudaStreamSynchronize(e->stream);
+    if (err == cudaSuccess) err = serr;
+    for (int i = 0; i < kSlots; ++i)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    if (pinned) cudaFreeHost(pinned);
+    munmap(map, fsize);
+    if (rc != B200_OK) return rc;
+    if (err != cudaSuccess) return from_cuda(err);
+    for (const GgufTensor &t : ts) mark_loaded(e, t.name);
     return B200_OK;
 }
 
@@ -946,13 +1201,23 @@ int b200_engine_set_precision(b200_engine *e, int32_t precision) {
     return B200_OK;
 }
 
-int b200_engine_inject_withhold(b200_engine *e, int32_t cta) {
-    if (!e || !e->finalized) return B200_ERR_INVALID_ARGUMENT;
+int b200_engine_inject_withhold(b200_engine *e, int32_t cta, int32_t after_steps) {
+    if (!e || !e->finalized || after_steps < 0) return B200_ERR_INVALID_ARGUMENT;
     if (!e->use_mk) return B200_ERR_NOT_SUPPORTED;
     if (cta >= mk_grid()) return B200_ERR_OUT_OF_RANGE;
     DeviceGuard dg(e->device);
-    const int32_t v = cta < 0 ? 0 : cta + 1;
-    B200_TRY(cudaMemcpyAsync(const_cast<int32_t *>(e->mk.withhold), &v, 4, cudaMemcpyHostToDevice, e->stream));
+    const int32_t v[2] = {cta < 0 ? 0 : cta + 1, cta < 0 ? 0 : after_steps};
+    B200_TRY(cudaMemcpyAsync(e->mk.withhold, v, 8, cudaMemcpyHostToDevice, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    return B200_OK;
+}
+
+int b200_engine_set_decode_launch_counter(b200_engine *e, uint64_t launches) {
+    if (!e || !e->finalized) return B200_ERR_INVALID_ARGUMENT;
+    if (!e->use_mk) return B200_ERR_NOT_SUPPORTED;
+    DeviceGuard dg(e->device);
+    const unsigned long long tickets = static_cast<unsigned long long>(launches) * mk_grid();
+    B200_TRY(cudaMemcpyAsync(e->mk.launches, &tickets, 8, cudaMemcpyHostToDevice, e->stream));
     B200_TRY(cudaStreamSynchronize(e->stream));
     return B200_OK;
 }
@@ -982,6 +1247,7 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
         e->pinned_io[0] = host_ids[0];
         B200_TRY(cudaMemcpyAsync(e->token, e->pinned_io, 4, cudaMemcpyHostToDevice, st));
         rc = build_graph(e);
+        if (rc == B200_OK) rc = mk_account(e, 1);
         if (rc != B200_OK) return rc;
         B200_TRY(cudaGraphLaunch(e->graph_exec, st));
     } else {
@@ -998,10 +1264,9 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
         B200_TRY(cudaMemcpyAsync(host_last_logits, e->logits, static_cast<size_t>(e->V) * 4, cudaMemcpyDeviceToHost, st));
     rc = check_status(e);  // synchronizes
     if (rc != B200_OK) {
-        // nothing committed: restore n_past
-        const int32_t np = static_cast<int32_t>(e->n_past);
-        cudaMemcpy(e->n_past_dev, &np, 4, cudaMemcpyHostToDevice);
-        return rc;
+        // nothing committed: restore n_past (a failed restore is the error reported)
+        const int rr = restore_n_past(e);
+        return rr != B200_OK ? rr : rc;
     }
     if (host_token) *host_token = e->pinned_io[e->io_tok];
     e->n_past += n;
@@ -1015,13 +1280,29 @@ int b200_engine_generate(b200_engine *e, int64_t n_steps, int32_t *host_tokens) 
     DeviceGuard dg(e->device);
     cudaStream_t st = e->stream;
     int rc = build_graph(e);
+    if (rc == B200_OK) rc = mk_account(e, n_steps);
     if (rc != B200_OK) return rc;
+    // the input token, restored if a step fails (each completed step advances the
+    // device token and n_past)
+    int32_t *saved_tok = e->pinned_io + e->io_tok + 2;
+    B200_TRY(cudaMemcpyAsync(saved_tok, e->token, 4, cudaMemcpyDeviceToHost, st));
     B200_TRY(cudaMemsetAsync(e->log_pos, 0, 4, st));
     for (int64_t i = 0; i < n_steps; ++i) B200_TRY(cudaGraphLaunch(e->graph_exec, st));
     if (host_tokens && n_steps > 0)
         B200_TRY(cudaMemcpyAsync(host_tokens, e->token_log, n_steps * 4, cudaMemcpyDeviceToHost, st));
     rc = check_status(e);
-    if (rc != B200_OK) return rc;
+    if (rc != B200_OK) {
+        // Nothing is committed: the steps before the failing one advanced the device
+        // n_past and token; both go back to the state before the call, so the next
+        // eval / generate continues from the last committed position (the KV rows
+        // those steps wrote are overwritten then).
+        int rr = restore_n_past(e);
+        if (rr == B200_OK) {
+            const cudaError_t ce = cudaMemcpyAsync(e->token, saved_tok, 4, cudaMemcpyHostToDevice, st);
+            rr = from_cuda(ce == cudaSuccess ? cudaStreamSynchronize(st) : ce);
+        }
+        return rr != B200_OK ? rr : rc;
+    }
     e->n_past += n_steps;
     return B200_OK;
 }
@@ -1105,7 +1386,8 @@ int b200_engine_trace_step(b200_engine *e, unsigned long long *host_trace, int m
         if (e->use_mk) {
             MkParams p = e->mk;
             p.trace = e->trace_buf;
-            rc = from_cuda(mk_launch(p, st));
+            rc = mk_account(e, 1);
+            if (rc == B200_OK) rc = from_cuda(mk_launch(p, st));
             n = 5 * e->c.n_layer + 1;
         } else {
             rc = enqueue_small_step(e, e->token, 1, false, 1, true);

@@ -348,13 +348,12 @@ bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int
 template <int EPI, int BN>
 cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a, int64_t n_tiles,
                        cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<EPI, BN>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(TCfg<BN>::kSmem));
+    {
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(gemm_tf32_kernel<EPI, BN>), ATTR_SMEM, [] {
+            return cudaFuncSetAttribute(gemm_tf32_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(TCfg<BN>::kSmem));
+        });
         if (e != cudaSuccess) return e;
-        attr_set = true;
     }
     const dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_tiles, device_sm_count())));
     return b200_launch(gemm_tf32_kernel<EPI, BN>, grid, dim3(kTThreads), TCfg<BN>::kSmem, st, pdl, mx, mw, a, n_tiles);

@@ -335,11 +335,11 @@ gemv_kernel(const GemvArgs a, const int rpc, const int stages, const uint32_t st
 template <int M, int EPI>
 cudaError_t launch_typed(const GemvArgs &a, const Layout &L, int grid, cudaStream_t stream, bool pdl) {
     auto kern = gemv_kernel<M, EPI>;
-    static bool configured = false;  // per instantiation; smem opt-in is device-wide state
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(kern), ATTR_SMEM, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        });
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     return b200_launch(kern, dim3(grid), dim3(kThreads), L.smem, stream, pdl, a, L.rpc, L.stages,
                        L.stage_floats, static_cast<uint32_t>(L.off_x),
@@ -361,14 +361,23 @@ cudaError_t launch_m(const GemvArgs &a, const Layout &L, int grid, cudaStream_t 
 }  // namespace
 
 int device_sm_count() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-            sms = 148;
+    // per device (grids are sized from the SM count of the device they run on)
+    constexpr int kMaxDev = 64;
+    static int sms[kMaxDev] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+        cudaGetLastError();
+        return 148;
     }
-    return sms;
+    if (!sms[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        sms[dev] = n;
+    }
+    return sms[dev];
 }
 
 int gemv_grid_size(int64_t N, int epi) {

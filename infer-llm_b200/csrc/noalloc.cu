@@ -9,8 +9,6 @@
 // This entry point serves them. Its scratch is a file-scope __device__ array of
 // B200_ARGMAX_NOALLOC_SCRATCH bytes that every GPU loading the library holds
 // until exit; every call shares it.
-#include <mutex>
-
 #include "elementwise.cuh"
 
 namespace {
@@ -18,25 +16,18 @@ namespace {
 constexpr size_t kScratchBytes = B200_ARGMAX_NOALLOC_SCRATCH;
 __device__ __align__(256) unsigned char g_argmax_scratch[kScratchBytes];
 
-// Device addresses of g_argmax_scratch, resolved once per device. In host code the
-// array's name is only a host-side stand-in, never a device address.
-constexpr int kMaxDevices = 64;
-void *g_scratch_ptr[kMaxDevices] = {};
-std::mutex g_scratch_mu;
-
+// The device address of g_argmax_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, never a device address. It is looked
+// up on every call (a cheap query once the module is loaded), so it stays right
+// after a device reset reloads the module at another address. The first call on a
+// device loads the module there; make it before any stream capture.
 int scratch_for_current_device(void **out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_ERR_CUDA;
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) {
-            cudaGetLastError();
-            return B200_ERR_CUDA;
-        }
-        g_scratch_ptr[dev] = p;
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return B200_ERR_CUDA;
     }
-    *out = g_scratch_ptr[dev];
+    *out = p;
     return B200_OK;
 }
 

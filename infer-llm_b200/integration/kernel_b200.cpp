@@ -16,6 +16,7 @@
 // RESHAPE are device copies, VIEW is a no-op (210-240, 305-326).
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "b200_infer.h"
 #include "kernels/cuda/kernel_f32.hpp"
@@ -37,6 +38,33 @@ cudaError_t as_cuda(int rc) {
 
 const float *cf(const Tensor *t) { return static_cast<const float *>(t->data); }
 float *mf(Tensor *t) { return static_cast<float *>(t->data); }
+
+// The decode attention's split workspace, one per device: the reference places
+// layers on several CUDA devices (src/model.cpp:400-437), and a kernel may only be
+// given memory of the device it runs on. Zero-filled when allocated, grown with the
+// context, and zeroed again after a call that failed (an aborted call can leave
+// split-merge counters behind; every completed call leaves them at zero).
+struct AttnWorkspace {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    bool dirty = false;
+};
+constexpr int kMaxDevices = 64;
+AttnWorkspace g_attn_ws[kMaxDevices];
+std::mutex g_attn_ws_mu;
+
+// Restores the current device on scope exit.
+struct CurrentDevice {
+    int prev = -1;
+    explicit CurrentDevice(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~CurrentDevice() {
+        int now = -1;
+        if (prev >= 0 && cudaGetDevice(&now) == cudaSuccess && now != prev) cudaSetDevice(prev);
+    }
+};
 
 }  // namespace
 
@@ -70,22 +98,36 @@ cudaError_t compute_flash_attn(Tensor *dst, cudaStream_t s) {
     const float scale = p.scale > 0.0f ? p.scale : 1.0f / std::sqrt(static_cast<float>(D));
     // Decode splits merge through a zero-filled workspace that later calls reuse; it
     // grows with the context (the reference kernel mallocs a score matrix per call,
-    // kernel_f32.cu:484-510). One backend thread drives the stream.
-    static void *ws = nullptr;
-    static size_t ws_bytes = 0;
+    // kernel_f32.cu:484-510). The workspace is the one of the device that holds q.
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, q->data) != cudaSuccess || pa.type != cudaMemoryTypeDevice ||
+        pa.device < 0 || pa.device >= kMaxDevices) {
+        cudaGetLastError();
+        return cudaErrorInvalidValue;
+    }
+    CurrentDevice on(pa.device);
+    std::lock_guard<std::mutex> lock(g_attn_ws_mu);
+    AttnWorkspace &ws = g_attn_ws[pa.device];
     const size_t need = b200_flash_attn_workspace_bytes(D, q->dims[1], k->dims[1], q->dims[2], k->dims[2]);
-    if (need > ws_bytes) {
-        if (ws && cudaFree(ws) != cudaSuccess) return cudaErrorUnknown;
-        ws = nullptr;
-        ws_bytes = 0;
-        if (cudaMalloc(&ws, need) != cudaSuccess) return cudaErrorMemoryAllocation;
-        if (cudaMemsetAsync(ws, 0, need, s) != cudaSuccess) return cudaErrorUnknown;
-        ws_bytes = need;
+    if (need > ws.bytes) {
+        if (ws.ptr && cudaFree(ws.ptr) != cudaSuccess) return cudaErrorUnknown;
+        ws.ptr = nullptr;
+        ws.bytes = 0;
+        if (cudaMalloc(&ws.ptr, need) != cudaSuccess) return cudaErrorMemoryAllocation;
+        ws.bytes = need;
+        ws.dirty = true;
+    }
+    if (ws.dirty) {
+        if (cudaMemsetAsync(ws.ptr, 0, ws.bytes, s) != cudaSuccess) return cudaErrorUnknown;
+        ws.dirty = false;
     }
     // K / V are views of the cache: token stride strides[2], head stride strides[1] (bytes)
-    return as_cuda(b200_flash_attn(cf(q), cf(k), cf(v), mf(dst), D, q->dims[1], k->dims[1], q->dims[2], k->dims[2],
-                                   static_cast<int64_t>(p.n_ctx), scale, k->strides[2] / 4, k->strides[1] / 4,
-                                   v->strides[2] / 4, v->strides[1] / 4, ws, ws_bytes, s));
+    const cudaError_t rc =
+        as_cuda(b200_flash_attn(cf(q), cf(k), cf(v), mf(dst), D, q->dims[1], k->dims[1], q->dims[2], k->dims[2],
+                                static_cast<int64_t>(p.n_ctx), scale, k->strides[2] / 4, k->strides[1] / 4,
+                                v->strides[2] / 4, v->strides[1] / 4, ws.ptr, ws.bytes, s));
+    if (rc != cudaSuccess) ws.dirty = true;
+    return rc;
 }
 
 cudaError_t compute_get_rows(Tensor *dst, cudaStream_t s) {

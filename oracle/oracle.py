@@ -6,7 +6,10 @@ ctypes bindings for the two CPU checkers of the B200 kernels:
   reference CPU backend (oracle/cpu_ops.c), and
 * ``Ref``   -- oracle/_ref/libinferllm_ref.so, the reference engine itself built
   from its own sources by ``make -C oracle ref`` (present only where it was built;
-  the file travels with the repository snapshot but is never committed).
+  the file travels with the repository snapshot but is never committed), and
+* ``RefCuda`` -- oracle/_ref/libref_cuda_ops.so, the reference's own CUDA kernels
+  (src/kernels/cuda/kernel_f32.cu compiled for sm_100a by ``make -C oracle
+  ref-cuda``) over device buffers given as raw pointers.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import this module.
 All arrays are numpy, C-contiguous; shapes follow the reference (dims[0] fastest),
@@ -26,6 +29,9 @@ REF_LIB = os.path.join(HERE, "_ref", "libinferllm_ref.so")
 # the reference engine on its own CUDA backend with the B200 kernels swapped in
 # (oracle/Makefile `ref-b200`): the drop-in check, not a checker
 REF_B200_LIB = os.path.join(HERE, "_ref", "libinferllm_ref_b200.so")
+# the reference's own CUDA kernels (kernel_f32.cu for sm_100a, oracle/Makefile
+# `ref-cuda`): the GPU-side checker of the op tests
+REF_CUDA_LIB = os.path.join(HERE, "_ref", "libref_cuda_ops.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
@@ -339,3 +345,35 @@ class RefEngine:
         if tok < 0:
             raise RuntimeError(f"ref_engine_eval failed ({tok})")
         return tok
+
+
+class RefCuda:
+    """The reference's own CUDA kernels (CUDA_F32::compute_*, kernel_f32.cu) on
+    caller-owned device buffers: every argument named like a tensor is a device
+    pointer (int), `stream` a cudaStream_t (int, 0 = legacy). Each call synchronizes
+    the stream and raises on a CUDA error. RoPE positions must lie in [0, n_ctx):
+    the reference kernel traps on any other, so the caller keeps them in range."""
+
+    def __init__(self, path: str = REF_CUDA_LIB):
+        L = self.lib = C.CDLL(path)
+        vp = C.c_void_p
+        L.refc_mul_mat.argtypes = [vp, vp, vp, _i64, _i64, _i64, vp]
+        L.refc_rms_norm.argtypes = [vp, vp, vp, _i64, _i64, C.c_float, vp]
+        L.refc_rope.argtypes = [vp, vp, vp, _i64, vp, _i64, _i64, _i64, vp]
+        L.refc_flash_attn.argtypes = [vp, vp, vp, vp, _i64, _i64, _i64, _i64, _i64, _i64, C.c_float, vp]
+        L.refc_get_rows.argtypes = [vp, vp, vp, _i64, _i64, _i64, vp]
+        L.refc_silu.argtypes = [vp, vp, _i64, vp]
+        L.refc_add.argtypes = [vp, vp, vp, _i64, vp]
+        L.refc_mul.argtypes = [vp, vp, vp, _i64, vp]
+        for f in ("refc_mul_mat", "refc_rms_norm", "refc_rope", "refc_flash_attn", "refc_get_rows",
+                  "refc_silu", "refc_add", "refc_mul"):
+            getattr(L, f).restype = C.c_int
+
+    @staticmethod
+    def available(path: str = REF_CUDA_LIB) -> bool:
+        return os.path.exists(path)
+
+    def call(self, name: str, *args):
+        rc = getattr(self.lib, "refc_" + name)(*args)
+        if rc != 0:
+            raise RuntimeError(f"reference CUDA kernel {name}: cudaError {rc}")

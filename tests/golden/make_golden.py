@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import os
 import sys
+import tempfile
 import zlib
 
 import numpy as np
@@ -83,7 +84,7 @@ def main():
 
     # end to end: tiny Qwen3, seed 7, prompt of 12 ids, 16 greedy steps
     cfg = G.QWEN3_TINY
-    path = os.path.join("/tmp", "b200_golden_tiny.gguf")
+    path = os.path.join(tempfile.mkdtemp(prefix="b200_golden_"), "tiny.gguf")
     G.write_gguf(path, cfg, seed=7)
     with open(path, "rb") as fh:
         g["e2e_gguf_crc32"] = np.array([zlib.crc32(fh.read())], np.uint32)

@@ -130,28 +130,58 @@ def test_engine_errors_leave_state_unchanged(cuda, tiny):
 def test_stopped_cta_is_reported_and_engine_recovers(cuda, tiny):
     """Failure detection of the single-launch decode step without a GPU fault: one
     CTA withholds its layer-0 QKV outputs (as if it had stopped), the CTAs waiting
-    for them give up after their bounded wait, the step reports B200_ERR_TIMEOUT and
-    commits nothing, and the same engine then reproduces the clean run."""
+    for them give up after their bounded wait, the call reports B200_ERR_TIMEOUT and
+    commits nothing, and the same engine continues -- without a reset -- exactly as
+    the clean run does. Injected at step 3 of generate(5) (two steps complete on the
+    device first, so n_past and the fed-back token must be rolled back) and at the
+    first step of a single-token eval."""
     import time
     cfg = G.QWEN3_TINY
     eng = B.Engine(cfg, kv_capacity=64, max_batch=16, decode_mode=B.DECODE_SINGLE).load_gguf(tiny).finalize()
     prompt = np.array([5, 17, 99, 3, 250, 8], np.int32)
-    clean = [eng.eval(prompt)] + [int(t) for t in eng.generate(4)]
+    clean = [eng.eval(prompt)] + [int(t) for t in eng.generate(10)]
     eng.reset()
     first = eng.eval(prompt)
     assert first == clean[0]
     lib = B.lib()
-    assert lib.b200_engine_inject_withhold(eng.h, 1) == 0
+    assert lib.b200_engine_inject_withhold(eng.h, 1, 2) == 0  # steps 1, 2 pass; step 3 fails
     t0 = time.perf_counter()
     with pytest.raises(B.B200Error) as e:
-        eng.generate(1)
+        eng.generate(5)
     assert e.value.status == 7  # B200_ERR_TIMEOUT
     assert time.perf_counter() - t0 < 30.0
     assert eng.n_past == len(prompt)  # nothing committed
-    assert lib.b200_engine_inject_withhold(eng.h, -1) == 0
+    assert lib.b200_engine_inject_withhold(eng.h, -1, 0) == 0
+    # no reset: generation continues from the last committed token and position
+    got = [int(t) for t in eng.generate(5)]
+    assert got == clean[1:6]
+    assert eng.n_past == len(prompt) + 5
+    # a failing single-token eval leaves the sequence where it was as well
+    assert lib.b200_engine_inject_withhold(eng.h, 1, 0) == 0
+    with pytest.raises(B.B200Error) as e:
+        eng.eval(np.array([clean[5]], np.int32))
+    assert e.value.status == 7
+    assert eng.n_past == len(prompt) + 5
+    assert lib.b200_engine_inject_withhold(eng.h, -1, 0) == 0
+    assert eng.eval(np.array([clean[5]], np.int32)) == clean[6]
+    assert [int(t) for t in eng.generate(4)] == clean[7:11]
+    eng.close()
+
+
+@pytest.mark.parametrize("start", [(1 << 24) - 4, (1 << 32) // 148 - 2], ids=["tag_period", "u32_tickets"])
+def test_decode_tags_across_counter_wrap(cuda, tiny, start):
+    """The single-launch decode step derives its exchange tags from a launch counter.
+    Started just before the tag period wraps (2^24 - 1 launches) and just before the
+    ticket count passes 2^32 (where a 32-bit counter would wrap to a launch number
+    that differs between CTAs), the generated tokens stay those of a fresh engine."""
+    cfg = G.QWEN3_TINY
+    eng = B.Engine(cfg, kv_capacity=64, max_batch=16, decode_mode=B.DECODE_SINGLE).load_gguf(tiny).finalize()
+    prompt = np.array([11, 2, 300, 77, 5], np.int32)
+    clean = [eng.eval(prompt)] + [int(t) for t in eng.generate(12)]
     eng.reset()
-    again = [eng.eval(prompt)] + [int(t) for t in eng.generate(4)]
-    assert again == clean
+    assert B.lib().b200_engine_set_decode_launch_counter(eng.h, start) == 0
+    got = [eng.eval(prompt)] + [int(t) for t in eng.generate(12)]
+    assert got == clean
     eng.close()
 
 
