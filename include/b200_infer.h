@@ -191,6 +191,10 @@ typedef struct b200_qwen3_config {
      * single-launch kernel where the shape allows it on one GPU, else the
      * multi-kernel chain) or B200_DECODE_MULTI (always the multi-kernel chain) */
     int32_t decode_mode;
+    /* 1: the engine allocates no KV cache; the caller binds each layer's KV object
+     * (b200_engine_bind_kv) before finalize, e.g. the reference's KV storage
+     * objects. 0: the engine owns a KV arena of kv_capacity tokens. */
+    int32_t external_kv;
 } b200_qwen3_config;
 
 #define B200_DECODE_AUTO 0
@@ -250,6 +254,28 @@ int b200_engine_decode_launches(const b200_engine *e);
  * Sampler::sample, sampler.cpp:5-65). On error nothing is committed. */
 int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n,
                      float *host_last_logits, int32_t *host_token);
+
+/* As b200_engine_eval, but the last row's logits (nullable) go to device memory of
+ * the engine's device (the logits tensor of a reference graph, for example). */
+int b200_engine_eval_device(b200_engine *e, const int32_t *host_ids, int64_t n,
+                            float *dev_last_logits, int32_t *host_token);
+
+/* Sets the sequence position (tokens already in the KV cache; <= kv_capacity), for
+ * a caller that keeps its own KV bookkeeping (the reference's KVCacheManager). */
+int b200_engine_set_n_past(b200_engine *e, int64_t n_past);
+
+/* Rotation frequencies freq[j], j < head_dim / 2 (host memory), replacing those the
+ * engine derived from rope_theta; the angle of position p stays
+ * float(double(p) * freq[j]). Row 1 of the reference's angle table
+ * (GraphContext::get_rope_theta_table, graph.cpp:92-135) is exactly freq. */
+int b200_engine_set_rope_freqs(b200_engine *e, const float *host_freq);
+
+/* external_kv engines: layer `layer` reads and appends K/V in the KV object at
+ * k_base / v_base (device memory of the engine's device, 16-byte aligned; token-major
+ * [kv_capacity][n_head_kv][head_dim] floats each, the NaiveKVStorage layout,
+ * naiveKVStorage.cpp:28-40). May be called again after finalize to move to another
+ * sequence's objects (the decode graph is captured again at the next step). */
+int b200_engine_bind_kv(b200_engine *e, int32_t layer, float *k_base, float *v_base);
 
 /* Greedy decode of n_steps tokens entirely on the device: each step feeds the
  * previous step's token back (CUDA-graph replay, no host round trip); the first

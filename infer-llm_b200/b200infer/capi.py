@@ -76,6 +76,10 @@ _SIGS = {
     "b200_engine_read_status": ([_vp, _vp], C.c_int),
     "b200_engine_load_gguf": ([_vp, C.c_char_p, C.c_int64], C.c_int),
     "b200_engine_get_weight": ([_vp, C.c_char_p, _vp, C.c_int64], C.c_int),
+    "b200_engine_eval_device": ([_vp, _vp, C.c_int64, _vp, _vp], C.c_int),
+    "b200_engine_set_n_past": ([_vp, C.c_int64], C.c_int),
+    "b200_engine_set_rope_freqs": ([_vp, _vp], C.c_int),
+    "b200_engine_bind_kv": ([_vp, C.c_int32, _vp, _vp], C.c_int),
     "b200_engine_inject_withhold": ([_vp, C.c_int32, C.c_int32], C.c_int),
     "b200_engine_set_decode_launch_counter": ([_vp, C.c_uint64], C.c_int),
     "b200_tp_unique_id": ([_vp], C.c_int),

@@ -15,7 +15,7 @@ class _Cfg(C.Structure):
                 ("n_ff", C.c_int32), ("n_ctx_train", C.c_int32), ("rope_theta", C.c_float),
                 ("rms_eps", C.c_float), ("tied", C.c_int32), ("kv_capacity", C.c_int32),
                 ("max_batch", C.c_int32), ("precision", C.c_int32), ("tp_rank", C.c_int32),
-                ("tp_world", C.c_int32), ("decode_mode", C.c_int32)]
+                ("tp_world", C.c_int32), ("decode_mode", C.c_int32), ("external_kv", C.c_int32)]
 
 DECODE_AUTO, DECODE_MULTI, DECODE_SINGLE = 0, 1, 2
 
@@ -38,7 +38,7 @@ class Engine:
         self.cfg = cfg
         self._c = _Cfg(cfg.n_vocab, cfg.n_embd, cfg.n_layer, cfg.n_head, cfg.n_head_kv, cfg.head_dim,
                        cfg.n_ff, cfg.n_ctx_train, cfg.rope_theta, cfg.rms_eps, int(cfg.tied),
-                       kv_capacity, max_batch, precision, tp_rank, tp_world, decode_mode)
+                       kv_capacity, max_batch, precision, tp_rank, tp_world, decode_mode, 0)
         h = C.c_void_p()
         _chk("b200_engine_create", lib().b200_engine_create(C.byref(self._c), device, C.byref(h)))
         self.h = h

@@ -698,7 +698,8 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
 
     cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
     if (err == cudaSuccess) err = cudaMalloc(&e->w_arena, e->w_bytes);
-    if (err == cudaSuccess) err = cudaMalloc(&e->kv_arena, e->kv_bytes);
+    if (c.external_kv) e->kv_bytes = 0;  // the caller binds each layer's KV object (b200_engine_bind_kv)
+    if (err == cudaSuccess && e->kv_bytes) err = cudaMalloc(&e->kv_arena, e->kv_bytes);
     if (err == cudaSuccess) err = cudaMalloc(&e->act_arena, e->act_bytes);
     e->io_tok = (static_cast<int64_t>(c.max_batch) + 15) / 16 * 16;
     if (err == cudaSuccess) err = cudaMallocHost(&e->pinned_io, static_cast<size_t>(e->io_tok + 16) * 4);
@@ -725,8 +726,10 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
         w.ffn_norm = wf(lo[l * 8 + 5]);
         w.wgu = wf(lo[l * 8 + 6]);
         w.wdown = wf(lo[l * 8 + 7]);
-        w.kc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l);
-        w.vc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l + kv_layer / 2);
+        if (e->kv_arena) {
+            w.kc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l);
+            w.vc = reinterpret_cast<float *>(e->kv_arena + kv_layer * l + kv_layer / 2);
+        }
     }
     e->x = af(o_x);
     e->xn = af(o_xn);
@@ -761,7 +764,7 @@ int b200_engine_create(const b200_qwen3_config *cfg, int device, b200_engine **o
     e->mk_words = e->act_arena + o_tx;
     e->mk_words_bytes = o_withhold - o_tx;  // the tagged words (tx .. tao)
     err = cudaMemsetAsync(e->act_arena, 0, e->act_bytes, e->stream);
-    if (err == cudaSuccess) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
+    if (err == cudaSuccess && e->kv_arena) err = cudaMemsetAsync(e->kv_arena, 0, e->kv_bytes, e->stream);
     std::vector<float> hf(D / 2);
     b200_rope_freqs(c.rope_theta, D, hf.data());
     if (err == cudaSuccess) err = cudaMemcpyAsync(e->freq, hf.data(), hf.size() * 4, cudaMemcpyHostToDevice, e->stream);
@@ -1141,6 +1144,11 @@ int b200_engine_finalize(b200_engine *e) {
         return B200_ERR_INVALID_ARGUMENT;
     }
     if (e->c.tp_world > 1 && !e->tp) return B200_ERR_INVALID_ARGUMENT;
+    for (const LayerW &w : e->L)
+        if (!w.kc || !w.vc) {
+            std::fprintf(stderr, "b200_engine_finalize: a layer's KV object is not bound\n");
+            return B200_ERR_INVALID_ARGUMENT;
+        }
     DeviceGuard dg(e->device);
     // Single-launch decode step where the shape allows it (one GPU only).
     MkParams &p = e->mk;
@@ -1228,8 +1236,15 @@ int b200_engine_decode_launches(const b200_engine *e) {
     return 5 * e->c.n_layer + 1 + (e->tp ? 2 : 0);
 }
 
-int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *host_last_logits,
-                     int32_t *host_token) {
+}  // extern "C"
+
+namespace {
+
+// One eval step; the last row's logits go to `last_logits` (host or, with
+// logits_on_device, device memory of this engine's device; nullable).
+int eval_to(b200_engine *e, const int32_t *host_ids, int64_t n, float *last_logits, bool logits_on_device,
+            int32_t *host_token) {
+    float *host_last_logits = last_logits;
     if (!e || !host_ids || n <= 0) return B200_ERR_INVALID_ARGUMENT;
     if (!e->finalized) return B200_ERR_INVALID_ARGUMENT;
     if (n > e->c.max_batch) return B200_ERR_INVALID_ARGUMENT;
@@ -1261,7 +1276,8 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
     }
     B200_TRY(cudaMemcpyAsync(e->pinned_io + e->io_tok, e->token, 4, cudaMemcpyDeviceToHost, st));
     if (want_logits && e->c.tp_world == 1)
-        B200_TRY(cudaMemcpyAsync(host_last_logits, e->logits, static_cast<size_t>(e->V) * 4, cudaMemcpyDeviceToHost, st));
+        B200_TRY(cudaMemcpyAsync(last_logits, e->logits, static_cast<size_t>(e->V) * 4,
+                                 logits_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
     rc = check_status(e);  // synchronizes
     if (rc != B200_OK) {
         // nothing committed: restore n_past (a failed restore is the error reported)
@@ -1270,6 +1286,59 @@ int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *
     }
     if (host_token) *host_token = e->pinned_io[e->io_tok];
     e->n_past += n;
+    return B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_engine_eval(b200_engine *e, const int32_t *host_ids, int64_t n, float *host_last_logits,
+                     int32_t *host_token) {
+    return eval_to(e, host_ids, n, host_last_logits, false, host_token);
+}
+
+int b200_engine_eval_device(b200_engine *e, const int32_t *host_ids, int64_t n, float *dev_last_logits,
+                            int32_t *host_token) {
+    return eval_to(e, host_ids, n, dev_last_logits, true, host_token);
+}
+
+int b200_engine_set_n_past(b200_engine *e, int64_t n_past) {
+    if (!e || n_past < 0 || n_past > e->c.kv_capacity) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    e->n_past = n_past;
+    return restore_n_past(e);
+}
+
+int b200_engine_set_rope_freqs(b200_engine *e, const float *host_freq) {
+    if (!e || !host_freq) return B200_ERR_INVALID_ARGUMENT;
+    DeviceGuard dg(e->device);
+    B200_TRY(cudaMemcpyAsync(e->freq, host_freq, static_cast<size_t>(e->D / 2) * 4, cudaMemcpyHostToDevice, e->stream));
+    B200_TRY(cudaStreamSynchronize(e->stream));
+    return B200_OK;
+}
+
+int b200_engine_bind_kv(b200_engine *e, int32_t layer, float *k_base, float *v_base) {
+    if (!e || !e->c.external_kv || layer < 0 || layer >= e->c.n_layer || !k_base || !v_base) return B200_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(k_base) | reinterpret_cast<uintptr_t>(v_base)) & 15) return B200_ERR_INVALID_ARGUMENT;
+    LayerW &w = e->L[layer];
+    if (w.kc == k_base && w.vc == v_base) return B200_OK;
+    DeviceGuard dg(e->device);
+    w.kc = k_base;
+    w.vc = v_base;
+    if (e->finalized) {
+        // the captured decode step holds the old KV addresses: capture it again at the
+        // next step; the single-launch step reads them from its device layer table
+        if (e->graph_exec) B200_TRY(cudaGraphExecDestroy(e->graph_exec));
+        if (e->graph) B200_TRY(cudaGraphDestroy(e->graph));
+        e->graph_exec = nullptr;
+        e->graph = nullptr;
+        if (e->use_mk) {
+            const MkLayer ml{w.attn_norm, w.wqkv, w.q_norm, w.k_norm, w.wo, w.ffn_norm, w.wgu, w.wdown, w.kc, w.vc};
+            B200_TRY(cudaMemcpyAsync(e->mk_layers + layer, &ml, sizeof ml, cudaMemcpyHostToDevice, e->stream));
+            B200_TRY(cudaStreamSynchronize(e->stream));
+        }
+    }
     return B200_OK;
 }
 
