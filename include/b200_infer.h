@@ -210,9 +210,11 @@ void b200_engine_destroy(b200_engine *e);
 /* Bytes the engine allocated, by arena (weights, kv, activations). */
 int b200_engine_memory(const b200_engine *e, size_t *weights, size_t *kv, size_t *act);
 
-/* Uploads one GGUF tensor (F32, host memory, numpy-style row-major (N, K)) by its
- * GGUF name, e.g. "blk.3.attn_q.weight". Under tensor parallelism the engine keeps
- * only its rank's shard of the full tensor passed here. */
+/* Uploads one GGUF tensor (F32, numpy-style row-major (N, K); host memory or device
+ * memory, told apart by unified addressing) by its GGUF name, e.g.
+ * "blk.3.attn_q.weight". Under tensor parallelism the engine keeps only its rank's
+ * shard of the full tensor passed here. Synchronous: the source may be released on
+ * return. */
 int b200_engine_set_weight(b200_engine *e, const char *name, const float *host_data,
                            int64_t n_elements);
 /* Loads every tensor of a GGUF v3 file (F32 tensors named as above) into the

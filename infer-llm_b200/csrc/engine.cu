@@ -890,7 +890,7 @@ int weight_block(b200_engine *e, const std::string &nm, int64_t n, WeightBlock *
 cudaError_t copy_rows(const WeightBlock &wb, float *host, int64_t a, int64_t b, cudaMemcpyKind kind, cudaStream_t st) {
     float *dev = wb.dst + a * wb.dpitch;
     float *hst = host + wb.src_off + a * wb.spitch;
-    if (kind == cudaMemcpyHostToDevice)
+    if (kind != cudaMemcpyDeviceToHost)
         return cudaMemcpy2DAsync(dev, wb.dpitch * 4, hst, wb.spitch * 4, wb.width * 4, b - a, kind, st);
     return cudaMemcpy2DAsync(hst, wb.spitch * 4, dev, wb.dpitch * 4, wb.width * 4, b - a, kind, st);
 }
@@ -980,8 +980,9 @@ int b200_engine_set_weight(b200_engine *e, const char *name, const float *host, 
     WeightBlock wb;
     const int rc = weight_block(e, name, n, &wb);
     if (rc != B200_OK) return rc;
-    cudaError_t err = copy_rows(wb, const_cast<float *>(host), 0, wb.rows, cudaMemcpyHostToDevice, e->stream);
-    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);  // host buffer may be released after return
+    // cudaMemcpyDefault: the source may be host memory or device memory (unified addressing)
+    cudaError_t err = copy_rows(wb, const_cast<float *>(host), 0, wb.rows, cudaMemcpyDefault, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);  // the source may be released after return
     if (err != cudaSuccess) return from_cuda(err);
     mark_loaded(e, name);
     return B200_OK;

@@ -29,6 +29,10 @@ REF_LIB = os.path.join(HERE, "_ref", "libinferllm_ref.so")
 # the reference engine on its own CUDA backend with the B200 kernels swapped in
 # (oracle/Makefile `ref-b200`): the drop-in check, not a checker
 REF_B200_LIB = os.path.join(HERE, "_ref", "libinferllm_ref_b200.so")
+# the reference engine with the B200 "cuda" Backend (integration/b200_backend.cpp) in
+# place of its CUDA backend (oracle/Makefile `ref-b200be`): the drop-in check of the
+# Backend seam, not a checker
+REF_B200BE_LIB = os.path.join(HERE, "_ref", "libinferllm_ref_b200be.so")
 # the reference's own CUDA kernels (kernel_f32.cu for sm_100a, oracle/Makefile
 # `ref-cuda`): the GPU-side checker of the op tests
 REF_CUDA_LIB = os.path.join(HERE, "_ref", "libref_cuda_ops.so")
@@ -235,6 +239,12 @@ class Ref:
         L.ref_engine_reset.restype = C.c_int
         L.ref_engine_eval.argtypes = [C.c_void_p, _i32p, _i64, C.c_void_p]
         L.ref_engine_eval.restype = C.c_int32
+        if hasattr(L, "ref_engine_backend"):
+            L.ref_engine_backend.argtypes = [C.c_void_p]
+            L.ref_engine_backend.restype = C.c_void_p
+        if hasattr(L, "b200_backend_counters"):
+            L.b200_backend_counters.argtypes = [C.c_void_p, C.POINTER(C.c_long), C.POINTER(C.c_long)]
+            L.b200_backend_counters.restype = C.c_int
         for fn in ("ref_mul_mat", "ref_rms_norm", "ref_rope_theta_table", "ref_rope",
                    "ref_flash_attn", "ref_silu", "ref_binary", "ref_get_rows"):
             getattr(L, fn).restype = C.c_int
@@ -337,6 +347,17 @@ class RefEngine:
     def reset(self):
         if self.ref.lib.ref_engine_reset(self.h) != 0:
             raise RuntimeError("ref_engine_reset failed")
+
+    def backend_counters(self):
+        """(steps run on the B200 engine, subgraphs run op by op) of the engine's
+        device backend, where the library registered the B200 Backend; else None."""
+        L = self.ref.lib
+        if not hasattr(L, "b200_backend_counters"):
+            return None
+        a, b = C.c_long(), C.c_long()
+        if L.b200_backend_counters(L.ref_engine_backend(self.h), C.byref(a), C.byref(b)) != 0:
+            return None
+        return a.value, b.value
 
     def eval(self, ids, logits: np.ndarray | None = None) -> int:
         ids = np.ascontiguousarray(ids, np.int32)

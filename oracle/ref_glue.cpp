@@ -323,6 +323,10 @@ int ref_engine_reset(void *h) {
     return 0;
 }
 
+// The device backend of an engine (null for a CPU engine): lets a test query the
+// backend a drop-in build registered (b200_backend_counters).
+void *ref_engine_backend(void *h) { return static_cast<RefEngine *>(h)->gpu.get(); }
+
 // One evaluation step (prefill when n > 1, decode when n == 1), the body of
 // bench.cpp Runner::evaluate. Writes the last row's logits (if non-null) and
 // returns the greedy token, or a negative code.
