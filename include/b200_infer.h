@@ -327,6 +327,11 @@ int b200_engine_read_status(b200_engine *e, int32_t *status);
  * ncclUniqueId (created by rank 0 with b200_tp_unique_id) before finalize. */
 int b200_tp_unique_id(unsigned char out_id[128]);
 int b200_engine_tp_init(b200_engine *e, const unsigned char id[128]);
+/* 1 if the engine's decode step exchanges its all-reduces and token selection over
+ * NVLink peer memory (its own kernels: CUDA IPC buffers, tagged words, bounded
+ * waits), 0 if over NCCL (a peer not reachable by peer access, or B200_TP_NCCL=1
+ * at tp_init). Prefill all-reduces always use NCCL. */
+int b200_engine_tp_peer_exchange(const b200_engine *e);
 
 #ifdef __cplusplus
 }

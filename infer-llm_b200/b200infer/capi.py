@@ -80,6 +80,7 @@ _SIGS = {
     "b200_engine_set_n_past": ([_vp, C.c_int64], C.c_int),
     "b200_engine_set_rope_freqs": ([_vp, _vp], C.c_int),
     "b200_engine_bind_kv": ([_vp, C.c_int32, _vp, _vp], C.c_int),
+    "b200_engine_tp_peer_exchange": ([_vp], C.c_int),
     "b200_engine_inject_withhold": ([_vp, C.c_int32, C.c_int32], C.c_int),
     "b200_engine_set_decode_launch_counter": ([_vp, C.c_uint64], C.c_int),
     "b200_tp_unique_id": ([_vp], C.c_int),

@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <tuple>
@@ -317,7 +318,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         o.trace = next_trace(e);
         std::tie(o.next_w, o.next_w_bytes) = wspan(5 * l + 4);
         B200_TRY(mark(e, "o_proj_gemv", gemv_launch(o, st, pdl)));
-        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st, pdl, e->status));
 
         GemvArgs gu;
         gu.w = w.wgu;
@@ -347,7 +348,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         dn.trace = next_trace(e);
         std::tie(dn.next_w, dn.next_w_bytes) = wspan(5 * l + 6);
         B200_TRY(mark(e, "down_gemv", gemv_launch(dn, st, pdl)));
-        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(M) * H, st, pdl, e->status));
     }
     GemvArgs lm;
     lm.w = e->lm_head;
@@ -369,7 +370,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
         lm.idx_offset = e->vocab_off;
         B200_TRY(gemv_launch(lm, st, pdl));
         B200_TRY(tp_select_token(e->tp, e->am_val + e->am_slots, e->am_idx + e->am_slots, e->tp_pairs, e->token, e->token_log,
-                                 e->log_pos, e->log_cap, e->n_past_dev, n_past_add, st));
+                                 e->log_pos, e->log_cap, e->n_past_dev, n_past_add, st, pdl, e->status));
     } else {
         lm.argmax_out = e->token;
         lm.token_log = e->token_log;
@@ -466,7 +467,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         o.ws_floats = e->gemm_ws_floats;
         o.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(o, st, pdl) : gemm_ffma_launch(o, st, pdl));
-        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st, false, e->status));
 
         B200_TRY(rms_norm_launch(e->x, w.ffn_norm, e->xn, H, n, e->c.rms_eps, st, pdl));
         GemmArgs gu;
@@ -499,7 +500,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         dn.ws_floats = e->gemm_ws_floats;
         dn.status = e->status;
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(dn, st, pdl) : gemm_ffma_launch(dn, st, pdl));
-        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st));
+        if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st, false, e->status));
     }
     GemvArgs lm;
     lm.w = e->lm_head;
@@ -521,7 +522,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         lm.idx_offset = e->vocab_off;
         B200_TRY(gemv_launch(lm, st, pdl));
         B200_TRY(tp_select_token(e->tp, e->am_val + e->am_slots, e->am_idx + e->am_slots, e->tp_pairs, e->token, e->token_log,
-                                 e->log_pos, e->log_cap, e->n_past_dev, n, st));
+                                 e->log_pos, e->log_cap, e->n_past_dev, n, st, false, e->status));
     } else {
         lm.argmax_out = e->token;
         lm.token_log = e->token_log;
@@ -542,10 +543,25 @@ int restore_n_past(b200_engine *e) {
     return B200_OK;
 }
 
+// Host wait bound of a tensor-parallel step (B200_TP_TIMEOUT_MS, default 60 s).
+int64_t tp_timeout_ms() {
+    const char *v = std::getenv("B200_TP_TIMEOUT_MS");
+    const long long x = (v && *v) ? std::atoll(v) : 60000;
+    return x > 0 ? x : 60000;
+}
+
 int check_status(b200_engine *e) {
-    int32_t s = 0;
-    B200_TRY(cudaMemcpyAsync(&s, e->status, 4, cudaMemcpyDeviceToHost, e->stream));
+    // into pinned memory: an asynchronous copy to pageable memory would block here
+    // until the stream drains, before the bounded wait below could begin
+    int32_t *ps = e->pinned_io + e->io_tok + 4;
+    *ps = 0;
+    B200_TRY(cudaMemcpyAsync(ps, e->status, 4, cudaMemcpyDeviceToHost, e->stream));
+    if (e->tp) {
+        const int rc = tp_sync(e->tp, e->stream, tp_timeout_ms());
+        if (rc != B200_OK) return rc;
+    }
     B200_TRY(cudaStreamSynchronize(e->stream));
+    const int32_t s = *ps;
     if (s == 0) return B200_OK;
     B200_TRY(cudaMemsetAsync(e->status, 0, 4, e->stream));
     // an aborted step may leave argmax tickets and attention split counters behind
@@ -1498,7 +1514,18 @@ int b200_tp_unique_id(unsigned char out_id[128]) { return tp_unique_id(out_id); 
 int b200_engine_tp_init(b200_engine *e, const unsigned char id[128]) {
     if (!e || !id || e->c.tp_world < 2) return B200_ERR_INVALID_ARGUMENT;
     DeviceGuard dg(e->device);
-    return tp_create(&e->tp, id, e->c.tp_rank, e->c.tp_world);
+    int rc = tp_create(&e->tp, id, e->c.tp_rank, e->c.tp_world);
+    if (rc != B200_OK) return rc;
+    // the decode path's all-reduces (at most 4 rows of H) and token selection over
+    // NVLink peer memory; NCCL where a peer is not reachable (B200_TP_NCCL=1 forces it)
+    const char *force = std::getenv("B200_TP_NCCL");
+    if (!(force && force[0] == '1')) {
+        rc = tp_p2p_init(e->tp, 4 * static_cast<int64_t>(e->H) + 2 * e->c.tp_world, e->stream);
+        if (rc != B200_OK && rc != B200_ERR_NOT_SUPPORTED) return rc;
+    }
+    return B200_OK;
 }
+
+int b200_engine_tp_peer_exchange(const b200_engine *e) { return e && e->tp && tp_p2p_ready(e->tp) ? 1 : 0; }
 
 }  // extern "C"
