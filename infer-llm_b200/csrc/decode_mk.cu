@@ -95,6 +95,17 @@ B200_DEVICE void rows_of(int64_t N, int unit, int b, int G, int64_t &r0, int64_t
     r1 = static_cast<int64_t>(units * static_cast<unsigned>(b + 1) / static_cast<unsigned>(G)) * unit;
 }
 
+// This CTA's geometry of one projection kind: its rows [r0, r1), rows per ring
+// chunk, chunks. The same in every layer, so it is computed once per launch (the
+// integer divisions behind it cost hundreds of cycles on the critical path when
+// redone at every phase). Index: PH_QKV, PH_O, PH_GU, PH_DOWN; kGeoLm = LM head.
+struct Geo {
+    int r0, r1, rpc, nch;
+};
+constexpr int kGeoLm = PH_ATTN;  // the attention slot holds the LM head (attention streams no weights)
+__shared__ Geo s_geo[PH_PER_LAYER];
+B200_DEVICE int geo_index(const MkParams &p, int l, int ph) { return l == p.n_layer ? kGeoLm : ph; }
+
 // Walks this CTA's weight schedule chunk by chunk, in consumption order: per layer
 // the QKV, o_proj, gate/up and down row slices (attention streams no weights), then
 // the LM head. A chunk is rpc whole rows (at most one ring stage). Advancing by n
@@ -104,11 +115,13 @@ struct Cursor {
     int64_t r0 = 0, r1 = 0;  // this CTA's rows of the phase; the cursor is at chunk k of nch
     PhaseW pw{};
 
-    B200_DEVICE void load_phase(const MkParams &p, int b, int G) {
+    B200_DEVICE void load_phase(const MkParams &p, int, int) {
         pw = phase_w(p, l, ph);
-        rows_of(pw.N, pw.unit, b, G, r0, r1);
-        rpc = rpc_for(pw.K, pw.unit);
-        nch = static_cast<int>((r1 - r0 + rpc - 1) / rpc);
+        const Geo &g = s_geo[geo_index(p, l, ph)];
+        r0 = g.r0;
+        r1 = g.r1;
+        rpc = g.rpc;
+        nch = g.nch;
     }
     // Positions the cursor at chunk n of the schedule; false if there is none.
     B200_DEVICE bool start(const MkParams &p, int b, int G, int n) {
@@ -489,32 +502,34 @@ struct Mk {
     // (schedule chunk cc + k) belongs to warp (cc + k) % kCW, which computes its
     // rpc whole rows (x from shared memory, one lane-strided pass, one warp
     // reduction per row) while the other warps work on the next chunks, and
-    // releases the slot to the producer. Row sums -> sm.part.
-    B200_DEVICE bool consume(const PhaseW &pw, int64_t r0, int64_t r1, int &cc, int trace_idx) {
+    // releases the slot to the producer. Row sums -> sm.part. With `out` set, the
+    // warp also publishes its rows at once (residual added from sm.res when
+    // `residual`): a phase's last row goes out as soon as it is computed, not after
+    // the CTA's barrier. Returns false on a failed wait (uniform over the CTA).
+    B200_DEVICE bool consume(const PhaseW &pw, const Geo &gm, int &cc, int trace_idx, u64 *out, uint32_t tag,
+                             bool residual) {
         const bool tr = p.trace && b == 0;  // CTA 0 records its slowest warp's chunk waits
         __shared__ unsigned long long s_wait, s_loop;
         if (tr && tid == 0) s_wait = s_loop = 0;
         uint64_t t_wait = 0;
         const long long tl0 = tr ? clock64() : 0;
-        const int rpc = rpc_for(pw.K, pw.unit);
+        const int rpc = gm.rpc, nch = gm.nch, r0 = gm.r0, r1 = gm.r1;
         const int K4 = static_cast<int>(pw.K >> 2);
-        const int64_t nch = (r1 - r0 + rpc - 1) / rpc;
         const uint32_t x_sa = smem_addr(sm.xs);
-        __shared__ int s_fail;
-        if (tid == 0) s_fail = 0;
-        named_sync(1, kCT);
+        bool failed = false;
+        if (tr) named_sync(1, kCT);  // s_wait / s_loop are cleared before any warp records
 #pragma unroll 1
-        for (int64_t k = ((warp - cc) % kCW + kCW) % kCW; k < nch; k += kCW) {
-            const int c = cc + static_cast<int>(k);
+        for (int k = ((warp - cc) % kCW + kCW) % kCW; k < nch; k += kCW) {
+            const int c = cc + k;
             const int s = c % kStages;
             const long long tw0 = tr ? clock64() : 0;
             if (!mbar_wait_bounded(&sm.full[s], (c / kStages) & 1, p.status)) {
-                s_fail = 1;
+                failed = true;
                 break;
             }
             if (tr) t_wait += clock64() - tw0;
-            const int64_t row = r0 + k * rpc;
-            const int rows = static_cast<int>(min64(rpc, r1 - row));
+            const int row = r0 + k * rpc;
+            const int rows = min(rpc, r1 - row);
             const uint32_t w_sa = smem_addr(sm.ring) + 4u * kStageFloats * s;
             float *dst = sm.part + (row - r0);
 #pragma unroll 1
@@ -528,21 +543,29 @@ struct Mk {
                 else
                     chunk_rows<1>(wr_sa, x_sa, K4, dst + r);
             }
-            __syncwarp();  // the stage is read: hand it back to the producer
+            __syncwarp();  // the stage is read (and lane 0's row sums are in sm.part)
             if (lane == 0) mbar_arrive(&sm.empty[s]);
+            if (out && lane < rows) {
+                float v = dst[lane];
+                if (residual) {  // this CTA's own residual rows, kept in shared memory
+                    v += sm.res[row - r0 + lane];
+                    sm.res[row - r0 + lane] = v;
+                }
+                st_tagged(out + row + lane, v, tag);
+            }
         }
-        cc += static_cast<int>(nch);
+        cc += nch;
         if (tr && lane == 0) {
             atomicMax(&s_wait, static_cast<unsigned long long>(t_wait));
             atomicMax(&s_loop, static_cast<unsigned long long>(clock64() - tl0));
         }
-        named_sync(1, kCT);
+        failed = named_sync_or(1, kCT, failed);
         if (tr && tid == 0) {
             p.trace[trace_idx * 8 + 1] = s_loop;        // slowest warp's ring loop, SM cycles
             p.trace[trace_idx * 8 + 6] = s_wait;        // slowest warp's total chunk wait, SM cycles
             p.trace[trace_idx * 8 + 7] = global_ns();   // all chunks consumed
         }
-        return s_fail == 0;  // uniform over the CTA
+        return !failed;
     }
 
     B200_DEVICE float row_sum(int64_t lr) const { return sm.part[lr]; }
@@ -945,6 +968,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mk_kernel(const MkParams p
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x, G = gridDim.x;
+    if (tid < PH_PER_LAYER) {  // this CTA's geometry of the four projections and the LM head
+        const PhaseW pw = phase_w(p, tid == kGeoLm ? p.n_layer : 0, tid);
+        int64_t r0 = 0, r1 = 0;
+        rows_of(pw.N, pw.unit, b, G, r0, r1);
+        const int rpc = rpc_for(pw.K, pw.unit);
+        s_geo[tid] = Geo{static_cast<int>(r0), static_cast<int>(r1), rpc, static_cast<int>((r1 - r0 + rpc - 1) / rpc)};
+    }
     if (tid == 0) {
         // every CTA of every launch takes one ticket: launch = ticket / G
         const unsigned long long ticket = atomicAdd(p.launches, 1ull);
@@ -1031,7 +1061,9 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
             continue;
         }
         const PhaseW pw = phase_w(p, l, ph);
-        rows_of(pw.N, pw.unit, b, G, r0, r1);
+        const Geo &gm = s_geo[geo_index(p, l, ph)];
+        r0 = gm.r0;
+        r1 = gm.r1;
         // phase input
         if (ph == PH_O) {
             ok = mk.load_act(p.tao, static_cast<int64_t>(p.Hq) * p.D, nullptr, mk.tag(l, PH_ATTN));
@@ -1048,27 +1080,21 @@ B200_DEVICE void run_step(Mk<D, GQ> &mk, const MkParams &p) {
         }
         if (!ok) break;
         stamp(p, q, 4);
-        ok = mk.consume(pw, r0, r1, cc, q);
-        if (l == p.n_layer) break;  // LM head: the argmax below
-        // epilogue: tagged outputs of this CTA's rows
-        const uint32_t mine = mk.tag(l, ph);
+        const bool lm_phase = l == p.n_layer;
+        const uint32_t mine = lm_phase ? 0u : mk.tag(l, ph);
+        // QKV / o_proj / down rows are published by the warp that computed them; the
+        // gate / up pairs of a SwiGLU row may sit in two chunks: after the barrier
+        u64 *early = (lm_phase || ph == PH_GU || (ph == PH_QKV && l == 0 && b == withheld)) ? nullptr
+                     : ph == PH_QKV                                                       ? p.tqkv
+                                                                                          : p.tx;
+        ok = mk.consume(pw, gm, cc, q, early, mine, ph != PH_QKV);
+        if (lm_phase) break;  // LM head: the argmax below
         if (ph == PH_GU) {
 #pragma unroll 1
             for (int64_t pr = r0 / 2 + tid; pr < r1 / 2; pr += kCT) {
                 const float gt = mk.row_sum(2 * pr - r0), up = mk.row_sum(2 * pr + 1 - r0);
                 const float sg = gt / (1.0f + expf(-gt));
                 st_tagged(p.th + pr, up * sg, mine);
-            }
-        } else if (!(ph == PH_QKV && l == 0 && b == withheld)) {
-            u64 *dst = ph == PH_QKV ? p.tqkv : p.tx;
-#pragma unroll 1
-            for (int64_t r = r0 + tid; r < r1; r += kCT) {
-                float v = mk.row_sum(r - r0);
-                if (ph != PH_QKV) {  // residual: this CTA's own rows, kept in shared memory
-                    v += mk.sm.res[r - r0];
-                    mk.sm.res[r - r0] = v;
-                }
-                st_tagged(dst + r, v, mine);
             }
         }
         stamp(p, q, 5);
