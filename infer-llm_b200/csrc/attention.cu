@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(2 * kDecThreads) attn_decode_kernel(const Attn
 constexpr int kD2Compute = 256;
 constexpr int kD2Threads = kD2Compute + 32;
 constexpr int kD2Tile = 32;
+constexpr int kD2KeysPerSplit = 128;  // keys a split takes (four tiles)
 
 template <int D>
 struct D2Cfg {
@@ -316,8 +317,14 @@ __global__ void __launch_bounds__(kD2Threads, 1)
     if (!a.early_kv) grid_wait();
     const int64_t n_past = a.n_past_dev ? static_cast<int64_t>(*a.n_past_dev) : a.n_past;
     const int64_t L = n_past + 1;
-    const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
-    const bool last = (s == S - 1);  // holds key n_past
+    // The grid has S splits for the longest context (the engine's graph is captured
+    // once); this step uses about kD2KeysPerSplit keys per split. Splits past SE exit
+    // at once, and with SE == 1 the one split writes the output itself (no workspace
+    // round trip, no counter).
+    const int SE = static_cast<int>(min64(S, max64(1, (L + kD2KeysPerSplit - 1) / kD2KeysPerSplit)));
+    if (s >= SE) return;
+    const int64_t j0 = L * s / SE, j1 = L * (s + 1) / SE;
+    const bool last = (s == SE - 1);  // holds key n_past
     const int ntiles = static_cast<int>((j1 - j0 + kD2Tile - 1) / kD2Tile);
     // In fused mode row n_past is produced by this kernel: patched from knew / vnew.
     const int64_t jload = fused ? min64(j1, n_past) : j1;
@@ -492,6 +499,24 @@ __global__ void __launch_bounds__(kD2Threads, 1)
         }
     }
     named_sync(1, kD2Compute);
+    if (SE == 1) {  // one split: the warps' merge is the output
+        for (int i = tid; i < G * D; i += kD2Compute) {
+            const int g = i / D;
+            float M = -INFINITY;
+            for (int w = 0; w < kD2Compute / 32; ++w) M = fmaxf(M, wp[w * WR + G * D + g]);
+            float lsum = 0.f, os = 0.f;
+            for (int w = 0; w < kD2Compute / 32; ++w) {
+                const float mw = wp[w * WR + G * D + g];
+                if (mw == -INFINITY) continue;
+                const float f = expf(mw - M);
+                lsum = fmaf(f, wp[w * WR + G * D + G + g], lsum);
+                os = fmaf(f, wp[w * WR + i], os);
+            }
+            a.out[(kvh * G) * D + i] = os / lsum;
+        }
+        tm.done();
+        return;
+    }
     unsigned *cnt = static_cast<unsigned *>(a.ws);
     float *ws = static_cast<float *>(a.ws) + d2_counter_words(a.Hkv);
     const size_t rec = static_cast<size_t>(G) * (D + 2);  // per (kvh, split): o [G][D], m [G], l [G]
@@ -516,7 +541,7 @@ __global__ void __launch_bounds__(kD2Threads, 1)
     }
     __threadfence();
     named_sync(1, kD2Compute);
-    if (tid == 0) s_last = atomicInc(cnt + kvh, static_cast<unsigned>(S - 1)) == static_cast<unsigned>(S - 1);
+    if (tid == 0) s_last = atomicInc(cnt + kvh, static_cast<unsigned>(SE - 1)) == static_cast<unsigned>(SE - 1);
     named_sync(1, kD2Compute);
     if (s_last) {
         __threadfence();
@@ -524,9 +549,9 @@ __global__ void __launch_bounds__(kD2Threads, 1)
         for (int i = tid; i < G * D; i += kD2Compute) {
             const int g = i / D;
             float M = -INFINITY;
-            for (int r = 0; r < S; ++r) M = fmaxf(M, __ldcg(all + r * rec + G * D + g));
+            for (int r = 0; r < SE; ++r) M = fmaxf(M, __ldcg(all + r * rec + G * D + g));
             float lsum = 0.f, o = 0.f;
-            for (int r = 0; r < S; ++r) {
+            for (int r = 0; r < SE; ++r) {
                 const float ms = __ldcg(all + r * rec + G * D + g);
                 if (ms == -INFINITY) continue;
                 const float f = expf(ms - M);
@@ -826,8 +851,8 @@ bool strides_ok(const AttnArgs &a) {
 }  // namespace
 
 int attn_decode_splits(int64_t max_len, int64_t Hkv) {
-    // About 128 keys (four tiles) per split, at most one CTA per SM over all KV heads.
-    int64_t s = (max_len + 127) / 128;
+    // About kD2KeysPerSplit keys (four tiles) per split, at most one CTA per SM over all KV heads.
+    int64_t s = (max_len + kD2KeysPerSplit - 1) / kD2KeysPerSplit;
     const int64_t cap = std::max<int64_t>(1, device_sm_count() / std::max<int64_t>(1, Hkv));
     s = std::min(s, cap);
     return static_cast<int>(std::max<int64_t>(1, s));
