@@ -45,8 +45,8 @@ SEED = 0
 # capture of `bench.py --steps 4 --warmup 3 --no-cpu-baseline` (positions ~36; the
 # per-step KV read grows by 229,376 bytes per position, weights are 2,384,199,680 of
 # it). TRAFFIC_SOURCE names the capture; the summary is under profiles/.
-TRAFFIC_PER_STEP = 2_395_436_000
-TRAFFIC_SOURCE = ("ncu --set full, one decode_mk_kernel launch of bench.py --steps 4 --warmup 3 "
+TRAFFIC_PER_STEP = 2_395_917_000
+TRAFFIC_SOURCE = ("ncu --set full, one decode_mk_kernel launch of bench.py --steps 4 --warmup 3, build 03b254aa2164 "
                   "(profiles/decode_mk_kernel_qwen3_0.6b_decode.md)")
 METRIC = "decode tok/s (Qwen3-0.6B-shape F32 bs1, 32-token prompt, greedy)"
 
