@@ -126,6 +126,36 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
 size_t b200_flash_attn_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64_t Tq,
                                        int64_t Tkv);
 
+/* Paged KV cache (the kernel side of a paged KVStrategy: KVCacheConfig::block_tokens
+ * > 0, include/kvcache/kvutil.hpp:43-44, which the reference declares but does not
+ * implement). K and V live in blocks of block_tokens tokens; k_blocks / v_blocks are
+ * device arrays of n_blocks device pointers, entry i the block of positions
+ * [i * block_tokens, (i + 1) * block_tokens) of the sequence, in the NaiveKVStorage
+ * layout with capacity block_tokens: element (token t of the block, KV head h, dim d)
+ * at block[(t * Hkv + h) * D + d]. The blocks may be anywhere (the reference's own
+ * storage objects, or slices of one pool).
+ *
+ * b200_paged_kv_write: the K / V rows of T new tokens (k_src, v_src: [T][Hkv][D] with
+ * token stride src_tok_stride floats, 16-byte aligned) into their blocks at positions
+ * pos0 .. pos0 + T - 1 (B200_ERR_OUT_OF_RANGE past n_blocks * block_tokens). */
+int b200_paged_kv_write(const float *k_src, const float *v_src, int64_t src_tok_stride,
+                        float *const *k_blocks, float *const *v_blocks, int64_t n_blocks,
+                        int64_t block_tokens, int64_t pos0, int64_t T, int64_t Hkv, int64_t D,
+                        int32_t *dev_status, void *stream);
+/* Causal GQA attention of q [Tq][Hq][D] against the paged cache's positions
+ * [0, Tkv) (Tkv = n_past + Tq, already written), out [Tq][Hq][D]; the same numerics
+ * contract as b200_flash_attn. Decode (Tq == 1) reads K / V through the block tables
+ * (split-KV, splits merged through the workspace; its counters must be zero before
+ * the first use, as for b200_flash_attn); Tq > 1 gathers [0, Tkv) into the workspace
+ * and runs the tiled prefill kernel. A null block pointer met on the way records
+ * B200_DEV_BAD_POSITION in dev_status and reads as zeros. head_dim 64 or 128. */
+int b200_flash_attn_paged(const float *q, const float *const *k_blocks, const float *const *v_blocks,
+                          int64_t n_blocks, int64_t block_tokens, float *out, int64_t D, int64_t Hq,
+                          int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past, float scale,
+                          void *workspace, size_t workspace_bytes, int32_t *dev_status, void *stream);
+size_t b200_flash_attn_paged_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64_t Tq,
+                                             int64_t Tkv);
+
 /* Elementwise ops of the reference graph (n elements).
  * CUDA_F32::compute_silu / compute_mul / compute_add (kernel_f32.cu:529-630). */
 int b200_silu(const float *x, float *out, int64_t n, void *stream);

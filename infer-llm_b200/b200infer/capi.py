@@ -81,6 +81,11 @@ _SIGS = {
     "b200_engine_set_rope_freqs": ([_vp, _vp], C.c_int),
     "b200_engine_bind_kv": ([_vp, C.c_int32, _vp, _vp], C.c_int),
     "b200_engine_tp_peer_exchange": ([_vp], C.c_int),
+    "b200_paged_kv_write": ([_vp, _vp, C.c_int64, _vp, _vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                             C.c_int64, _vp, _vp], C.c_int),
+    "b200_flash_attn_paged": ([_vp, _vp, _vp, C.c_int64, C.c_int64, _vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                               C.c_int64, C.c_int64, C.c_float, _vp, _sz, _vp, _vp], C.c_int),
+    "b200_flash_attn_paged_workspace_bytes": ([C.c_int64] * 5, _sz),
     "b200_engine_inject_withhold": ([_vp, C.c_int32, C.c_int32], C.c_int),
     "b200_engine_set_decode_launch_counter": ([_vp, C.c_uint64], C.c_int),
     "b200_tp_unique_id": ([_vp], C.c_int),
@@ -242,3 +247,41 @@ def argmax(logits, status=None):
     out = torch.empty(1, device=logits.device, dtype=torch.int32)
     _chk("b200_argmax", lib().b200_argmax(_p(logits), n, _p(out), _p(ws), ws.numel(), _p(status), _stream()))
     return out
+
+
+class PagedKV:
+    """A paged K/V cache on the device for tests and benchmarks: n_blocks blocks of
+    block_tokens tokens each (one torch tensor per pool; the block tables list the
+    blocks in `order`, so logical block i is pool block order[i])."""
+
+    def __init__(self, n_blocks, block_tokens, Hkv, D, device, order=None):
+        import torch
+        self.bt, self.Hkv, self.D = block_tokens, Hkv, D
+        self.kpool = torch.zeros((n_blocks, block_tokens, Hkv, D), device=device)
+        self.vpool = torch.zeros_like(self.kpool)
+        order = list(range(n_blocks)) if order is None else list(order)
+        bytes_per = block_tokens * Hkv * D * 4
+        self.ktab = torch.tensor([self.kpool.data_ptr() + i * bytes_per for i in order], dtype=torch.int64, device=device)
+        self.vtab = torch.tensor([self.vpool.data_ptr() + i * bytes_per for i in order], dtype=torch.int64, device=device)
+        self.n_blocks = len(order)
+
+    def write(self, k, v, pos0, status=None):
+        """k, v (T, Hkv, D) contiguous -> positions pos0..pos0+T-1."""
+        T = k.shape[0]
+        _chk("b200_paged_kv_write", lib().b200_paged_kv_write(
+            _p(k), _p(v), self.Hkv * self.D, _p(self.ktab), _p(self.vtab), self.n_blocks, self.bt, pos0, T,
+            self.Hkv, self.D, _p(status), _stream()))
+
+    def attn(self, q, n_past, scale=0.0, out=None, workspace=None, status=None):
+        """q (Tq, Hq, D) against positions [0, n_past + Tq)."""
+        import torch
+        Tq, Hq, D = q.shape
+        Tkv = n_past + Tq
+        out = out if out is not None else torch.empty_like(q)
+        nbytes = lib().b200_flash_attn_paged_workspace_bytes(D, Hq, self.Hkv, Tq, Tkv)
+        if workspace is None:
+            workspace = torch.zeros(nbytes, device=q.device, dtype=torch.uint8)
+        _chk("b200_flash_attn_paged", lib().b200_flash_attn_paged(
+            _p(q), _p(self.ktab), _p(self.vtab), self.n_blocks, self.bt, _p(out), D, Hq, self.Hkv, Tq, Tkv, n_past,
+            scale, _p(workspace), workspace.numel(), _p(status), _stream()))
+        return out

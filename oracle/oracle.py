@@ -239,6 +239,9 @@ class Ref:
         L.ref_engine_reset.restype = C.c_int
         L.ref_engine_eval.argtypes = [C.c_void_p, _i32p, _i64, C.c_void_p]
         L.ref_engine_eval.restype = C.c_int32
+        if hasattr(L, "ref_paged_kv_selftest"):
+            L.ref_paged_kv_selftest.argtypes = [_i64, _i64, _i64, _i64, C.c_void_p]
+            L.ref_paged_kv_selftest.restype = C.c_int
         if hasattr(L, "ref_engine_backend"):
             L.ref_engine_backend.argtypes = [C.c_void_p]
             L.ref_engine_backend.restype = C.c_void_p

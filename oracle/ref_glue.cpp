@@ -28,6 +28,7 @@
 #include "kvcache/kvcacheManager.hpp"
 #include "kvcache/KVStorages/naiveKVStorage.hpp"
 #include "kvcache/KVStrategys/contiguousKVStrategy.hpp"
+#include "paged_kv_strategy.hpp"
 
 #ifdef INFERLLM_WITH_CUDA
 #include <cuda_runtime_api.h>
@@ -320,6 +321,89 @@ int ref_engine_reset(void *h) {
     if (!seq) return -1;
     e->seq = *seq;
     if (!e->ctx->set_kv_cache(e->cache.get(), e->seq)) return -1;
+    return 0;
+}
+
+// Drives infer-llm_b200/integration/paged_kv_strategy.cpp through the reference's
+// own KVCacheManager + NaiveKVStorage on the CPU backend: two appends of `first` and
+// `second` tokens across block boundaries (views written and read back through the
+// manager's segment views), an aborted append (its blocks freed again), and the
+// block table the paged kernels take. Returns 0, or the number of the failed check.
+// out[0] = segments of the second append's readable view, out[1] = blocks held.
+int ref_paged_kv_selftest(int64_t block_tokens, int64_t n_layer, int64_t first, int64_t second, int64_t *out) {
+    Backend *cpu = cpu_backend(0);
+    if (!cpu) return 1;
+    Quiet q;
+    constexpr std::size_t Hkv = 2, D = 8, HD = Hkv * D;
+    std::vector<KVLayerSpec> layers(static_cast<size_t>(n_layer),
+                                    KVLayerSpec{.n_kv_heads = Hkv, .k_head_dim = D, .v_head_dim = D,
+                                                .k_type = GGML_TYPE_F32, .v_type = GGML_TYPE_F32});
+    auto strategy = std::make_unique<PagedKVStrategy>(std::make_unique<NaiveKVStorage>());
+    PagedKVStrategy *paged = strategy.get();
+    KVCacheManager mgr(std::move(strategy));
+    std::vector<Backend *> place(layers.size(), cpu);
+    KVCacheConfig cfg{.layers = layers.size(), .max_tokens_per_sequence = 4096,
+                      .block_tokens = static_cast<size_t>(block_tokens)};
+    if (!mgr.init(layers, place, cfg)) return 2;
+    auto seq = mgr.create_sequence();
+    if (!seq) return 3;
+    auto value = [](size_t layer, size_t pos, bool is_v) { return float(layer * 100000 + pos * 2 + (is_v ? 1 : 0)); };
+    // append [0, first) then [first, first + second); write the new rows through the
+    // writable segments, then read every row back through the readable segments
+    size_t done = 0;
+    for (int64_t n : {first, second}) {
+        if (!mgr.reserve_append(*seq, static_cast<size_t>(n))) return 4;
+        for (size_t l = 0; l < layers.size(); ++l) {
+            auto acc = mgr.acquire_layer(*seq, l);
+            if (!acc) return 5;
+            size_t pos = done;
+            for (size_t i = 0; i < acc->writable.k.size(); ++i) {
+                const KVSegmentView &ks = acc->writable.k[i], &vs = acc->writable.v[i];
+                if (ks.token_begin != pos || ks.token_count == 0 || ks.token_count > cfg.block_tokens) return 6;
+                for (size_t t = 0; t < ks.token_count; ++t)
+                    for (size_t e = 0; e < HD; ++e) {
+                        static_cast<float *>(ks.view.data)[t * HD + e] = value(l, pos + t, false);
+                        static_cast<float *>(vs.view.data)[t * HD + e] = value(l, pos + t, true);
+                    }
+                pos += ks.token_count;
+            }
+            if (pos != done + static_cast<size_t>(n)) return 7;
+            size_t rpos = 0;
+            for (size_t i = 0; i < acc->readable.k.size(); ++i) {
+                const KVSegmentView &ks = acc->readable.k[i], &vs = acc->readable.v[i];
+                if (ks.token_begin != rpos) return 8;
+                for (size_t t = 0; t < ks.token_count; ++t)
+                    for (size_t e = 0; e < HD; e += 7)
+                        if (static_cast<float *>(ks.view.data)[t * HD + e] != value(l, rpos + t, false) ||
+                            static_cast<float *>(vs.view.data)[t * HD + e] != value(l, rpos + t, true))
+                            return 9;
+                rpos += ks.token_count;
+            }
+            if (rpos != pos) return 10;
+            if (l == 0 && out) out[0] = static_cast<int64_t>(acc->readable.k.size());
+            if (!mgr.release_layer(*acc)) return 11;
+        }
+        if (!mgr.commit_append(*seq)) return 12;
+        done += static_cast<size_t>(n);
+    }
+    const size_t held = paged->blocks(*seq, 0);
+    if (held != (done + cfg.block_tokens - 1) / cfg.block_tokens) return 13;
+    // an aborted append gives its new blocks back
+    if (!mgr.reserve_append(*seq, cfg.block_tokens + 1)) return 14;
+    if (paged->blocks(*seq, 0) <= held) return 15;
+    if (!mgr.abort_append(*seq)) return 16;
+    if (paged->blocks(*seq, 0) != held) return 17;
+    // the kernels' block table: position p at k[p / bt] + (p % bt) * HD
+    std::vector<void *> kt, vt;
+    if (!paged->block_table(*seq, n_layer - 1, done, kt, vt)) return 18;
+    for (size_t p = 0; p < done; ++p) {
+        const float *kb = static_cast<const float *>(kt[p / cfg.block_tokens]);
+        const float *vb = static_cast<const float *>(vt[p / cfg.block_tokens]);
+        const size_t o = (p % cfg.block_tokens) * HD;
+        if (kb[o] != value(n_layer - 1, p, false) || vb[o + HD - 1] != value(n_layer - 1, p, true)) return 19;
+    }
+    if (out) out[1] = static_cast<int64_t>(held);
+    if (!mgr.release_sequence(*seq)) return 20;
     return 0;
 }
 
