@@ -29,6 +29,7 @@ constexpr int kPgWarps = kPgThreads / 32;
 constexpr int kPgKeys = 4;                    // keys per warp per batch
 constexpr int kPgBatch = kPgKeys * kPgWarps;  // 32 keys per CTA batch
 constexpr int kPgKeysPerSplit = 128;
+constexpr int kPgTab = 256;                   // block pointers a split stages in shared memory
 
 struct PagedArgs {
     const float *q = nullptr;                  // [Hq][D] (one token)
@@ -67,6 +68,8 @@ __global__ void __launch_bounds__(kPgThreads) attn_decode_paged_kernel(const Pag
     constexpr int E = D / 32;
     constexpr int WR = G * (D + 2);  // one warp's (o, m, l) record
     __shared__ float wp[kPgWarps * WR];
+    __shared__ const float *s_kb[kPgTab];
+    __shared__ const float *s_vb[kPgTab];
     __shared__ int s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = blockIdx.x;
@@ -90,6 +93,15 @@ __global__ void __launch_bounds__(kPgThreads) attn_decode_paged_kernel(const Pag
         }
     }
     bool bad = false;
+    // The split's block pointers, staged in shared memory once (a row load then
+    // needs no dependent global load of its block's address); a split spanning more
+    // than kPgTab blocks reads the rest from the tables.
+    const int64_t b0 = j0 / a.bt, nb = (j1 - 1) / a.bt - b0 + 1;
+    for (int64_t i = tid; i < min64(nb, kPgTab); i += kPgThreads) {
+        s_kb[i] = a.kb[b0 + i];
+        s_vb[i] = a.vb[b0 + i];
+    }
+    __syncthreads();
     // K / V rows of this warp's keys of the batch at `base` (zeros past j1)
     auto load = [&](int64_t base, float (&kv)[kPgKeys][E], float (&vv)[kPgKeys][E]) {
 #pragma unroll
@@ -98,8 +110,8 @@ __global__ void __launch_bounds__(kPgThreads) attn_decode_paged_kernel(const Pag
             const float *kp = nullptr, *vp = nullptr;
             if (j < j1) {
                 const int64_t blk = j / a.bt, off = j - blk * a.bt;
-                kp = a.kb[blk];
-                vp = a.vb[blk];
+                kp = blk - b0 < kPgTab ? s_kb[blk - b0] : a.kb[blk];
+                vp = blk - b0 < kPgTab ? s_vb[blk - b0] : a.vb[blk];
                 if (!kp || !vp) {
                     bad = true;
                     kp = vp = nullptr;

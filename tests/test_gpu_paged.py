@@ -108,7 +108,7 @@ def test_paged_missing_block_is_reported(cuda):
     assert int(status.item()) == 2  # B200_DEV_BAD_POSITION
     assert torch.isfinite(out).all()
     with pytest.raises(B.B200Error):  # past the blocks' positions
-        cache.write(k[:8].contiguous(), k[:8].contiguous(), L)
+        cache.write(k[:8].contiguous(), k[:8].contiguous(), cache.n_blocks * cache.bt - 4)
 
 
 def test_paged_decode_bandwidth(cuda):
@@ -129,6 +129,7 @@ def test_paged_decode_bandwidth(cuda):
         ts = []
         for _ in range(10):
             flush.zero_()
+            torch.cuda._sleep(200_000)  # the GPU stays busy while the host submits the call
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             fn()
