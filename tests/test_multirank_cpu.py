@@ -161,3 +161,54 @@ def test_bench_takes_max_over_ranks():
 def test_bench_max_over_ranks_single(world):
     import bench
     assert bench.max_over_ranks(3.25, world) == 3.25
+
+
+def _leaving_worker(rank, world, port, mode, out):
+    """Two tensor-parallel ranks take one decode step together; then rank 1 leaves
+    between steps (mode "exit": its process ends; "stall": it stays alive but never
+    joins the next step). Rank 0's next step must end with an error within the
+    process group's short timeout, not hang."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    w = _weights()
+
+    def allreduce(v):
+        t = torch.from_numpy(np.ascontiguousarray(v))
+        dist.all_reduce(t)
+        return t.numpy()
+
+    cache = [([], []) for _ in range(CFG.n_layer)]
+    logits = _step(w, 7, 0, cache, rank, world, allreduce)
+    tok = int(np.argmax(logits))
+    if rank == 1:
+        if mode == "stall":
+            time.sleep(8)  # alive, not joining, past rank 0's 5 s timeout
+        os._exit(0)  # no destroy_process_group: the rank is simply gone
+    t0 = time.monotonic()
+    try:
+        _step(w, tok, 1, cache, rank, world, allreduce)
+        out.put(("completed", time.monotonic() - t0))
+    except Exception as e:  # gloo reports the lost peer / the timeout
+        out.put((type(e).__name__, time.monotonic() - t0))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_tp_rank_leaving_between_steps_is_an_error(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        what, dt = q.get(timeout=60)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert what != "completed", "rank 0's step completed without its peer"
+    assert dt < 15.0, dt  # bounded by the 5 s process-group timeout, not a hang
