@@ -590,7 +590,7 @@ def run_op(args):
 
     --op gemv|gemm: y = x.W^T with W (N, K) ~ N(0, 0.02), x (M, K) ~ N(0, 1);
     --op attn: GQA attention (16 q / 8 kv heads, d 128), decode (--M 1, --L cache
-    length) or prefill (--M tokens, causal);
+    length) or prefill (--M tokens, causal; --precision 1: the tensor-core kernel);
     --op sweep: every shape of configs[1] (the six projection shapes of a layer plus
     the LM head at M = 1, 32, 256; M > 4 with the FFMA and the TF32 GEMM) and
     configs[2] (prefill S = 32..2048, decode L = 256..8192) in one process.
@@ -611,7 +611,8 @@ def run_op(args):
                     for prec in (0, 1):
                         cases.append(dict(op="gemm", K=K, N=N, M=M, L=0, precision=prec))
         for S in (32, 64, 128, 256, 2048):
-            cases.append(dict(op="attn", K=0, N=0, M=S, L=S, precision=0))
+            for prec in (0, 1):
+                cases.append(dict(op="attn", K=0, N=0, M=S, L=S, precision=prec))
         for L in (256, 1024, 4096, 8192):
             cases.append(dict(op="attn", K=0, N=0, M=1, L=L, precision=0))
     else:
@@ -634,7 +635,8 @@ def op_case(c, steps, warmup):
         w = torch.randn((N, K), device=dev, generator=g) * 0.02
         x = torch.randn((M, K), device=dev, generator=g)
         out = torch.empty((M, N), device=dev)
-        fn = lambda: B.mul_mat(w, x, precision=c["precision"], out=out)
+        ws = torch.empty(B.lib().b200_mul_mat_workspace_bytes(K, N, M, c["precision"]), dtype=torch.uint8, device=dev)
+        fn = lambda: B.mul_mat(w, x, precision=c["precision"], out=out, workspace=ws)
         nbytes = 4 * (N * K + M * K + M * N)
         flops = 2 * M * N * K
     else:
@@ -647,7 +649,7 @@ def op_case(c, steps, warmup):
         v = torch.randn((L, Hkv, D), device=dev, generator=g)
         out = torch.empty_like(q)
         ws = torch.zeros(B.lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, M, L), dtype=torch.uint8, device=dev)
-        fn = lambda: B.flash_attn(q, k, v, n_past, out=out, workspace=ws)
+        fn = lambda: B.flash_attn(q, k, v, n_past, out=out, workspace=ws, precision=c["precision"])
         nbytes = 4 * (2 * L * Hkv * D + 2 * M * Hq * D)
         causal_pairs = M * n_past + M * (M + 1) / 2
         flops = 4 * Hq * D * causal_pairs

@@ -69,6 +69,15 @@ int b200_device_supported(int device);
  * uses the tiled GEMM selected by `precision`. */
 int b200_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
                  int precision, void *stream);
+/* b200_mul_mat with a split-K workspace: where the M x N tiles leave SMs idle
+ * (prompts up to a few hundred tokens on the layer shapes) K is split across CTAs,
+ * each split's partial sums go to the workspace and are added in split order
+ * (deterministic), so every SM takes part. `workspace` (16-byte aligned, contents
+ * ignored) of b200_mul_mat_workspace_bytes(K, N, M, precision) bytes enables every
+ * split; a smaller one fewer, NULL none. */
+int b200_mul_mat_ws(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
+                    int precision, void *workspace, size_t workspace_bytes, void *stream);
+size_t b200_mul_mat_workspace_bytes(int64_t K, int64_t N, int64_t M, int precision);
 
 /* Row-wise RMSNorm over D contiguous floats: y = x * rsqrt(mean(x^2) + eps) * gamma.
  * Replaces CUDA_F32::compute_rms_norm (kernel_f32.hpp:14, kernel_f32.cu:60-90). */
@@ -125,6 +134,15 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
                     size_t workspace_bytes, void *stream);
 size_t b200_flash_attn_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64_t Tq,
                                        int64_t Tkv);
+/* b200_flash_attn with a precision for Tq > 1: B200_PREC_FFMA (exact F32, as
+ * b200_flash_attn) or B200_PREC_TF32 (head_dim 128: S = Q K^T and O = P V on the
+ * tcgen05 tensor cores with TF32 inputs and F32 accumulation, scores and O in tensor
+ * memory; other head sizes fall back to the exact kernel). Decode is unaffected. */
+int b200_flash_attn_ex(const float *q, const float *k, const float *v, float *out, int64_t D,
+                       int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past,
+                       float scale, int64_t k_tok_stride, int64_t k_head_stride,
+                       int64_t v_tok_stride, int64_t v_head_stride, void *workspace,
+                       size_t workspace_bytes, void *stream, int32_t precision);
 
 /* Paged KV cache (the kernel side of a paged KVStrategy: KVCacheConfig::block_tokens
  * > 0, include/kvcache/kvutil.hpp:43-44, which the reference declares but does not

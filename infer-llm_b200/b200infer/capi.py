@@ -41,6 +41,8 @@ _SIGS = {
     "b200_status_string": ([C.c_int], C.c_char_p),
     "b200_device_supported": ([C.c_int], C.c_int),
     "b200_mul_mat": ([_vp, _vp, _vp, _i64, _i64, _i64, C.c_int, _vp], C.c_int),
+    "b200_mul_mat_ws": ([_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _sz, _vp], C.c_int),
+    "b200_mul_mat_workspace_bytes": ([_i64, _i64, _i64, _i32], _sz),
     "b200_rms_norm": ([_vp, _vp, _vp, _i64, _i64, _f32, _vp], C.c_int),
     "b200_rope": ([_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp], C.c_int),
     "b200_qk_norm_rope": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64,
@@ -48,6 +50,8 @@ _SIGS = {
     "b200_rope_freqs": ([_f32, _i64, _vp], None),
     "b200_flash_attn": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i64, _i64, _i64,
                          _i64, _vp, _sz, _vp], C.c_int),
+    "b200_flash_attn_ex": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i64, _i64, _i64,
+                            _i64, _vp, _sz, _vp, _i32], C.c_int),
     "b200_flash_attn_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64], _sz),
     "b200_silu": ([_vp, _vp, _i64, _vp], C.c_int),
     "b200_mul": ([_vp, _vp, _vp, _i64, _vp], C.c_int),
@@ -128,14 +132,23 @@ def _dev_check(*ts):
             assert t.is_cuda and t.is_contiguous(), "expected contiguous CUDA tensors"
 
 
-def mul_mat(w, x, precision=PREC_FFMA, out=None):
-    """y = x . w^T; w (N, K), x (M, K) -> (M, N) float32."""
+def mul_mat(w, x, precision=PREC_FFMA, out=None, workspace=None):
+    """y = x . w^T; w (N, K), x (M, K) -> (M, N) float32.
+
+    workspace: a uint8 tensor of b200_mul_mat_workspace_bytes bytes for the split-K
+    partials (None: one is allocated when the shape splits K; an empty tensor: no
+    split)."""
     import torch
     _dev_check(w, x)
     N, K = w.shape
     M = x.shape[0]
     out = out if out is not None else torch.empty((M, N), device=x.device, dtype=torch.float32)
-    _chk("b200_mul_mat", lib().b200_mul_mat(_p(w), _p(x), _p(out), K, N, M, precision, _stream()))
+    if workspace is None:
+        nbytes = lib().b200_mul_mat_workspace_bytes(K, N, M, precision)
+        workspace = torch.empty(nbytes, device=x.device, dtype=torch.uint8)
+    _chk("b200_mul_mat_ws", lib().b200_mul_mat_ws(_p(w), _p(x), _p(out), K, N, M, precision,
+                                                  _p(workspace) if workspace.numel() else None,
+                                                  workspace.numel(), _stream()))
     return out
 
 
@@ -182,12 +195,13 @@ def qk_norm_rope(q, k, q_gamma, k_gamma, freq, pos, eps, n_ctx, v=None, k_out=No
     return q_out, k_out, v_out
 
 
-def flash_attn(q, k, v, n_past, scale=0.0, out=None, workspace=None):
+def flash_attn(q, k, v, n_past, scale=0.0, out=None, workspace=None, precision=0):
     """q (Tq, Hq, D); k, v (Tkv, Hkv, D) token-major; returns (Tq, Hq, D).
 
     workspace: a zero-filled uint8 tensor of b200_flash_attn_workspace_bytes bytes
     (reusable across calls), or None for a fresh one; pass an empty tensor to run
-    decode without one (the cluster-merged path)."""
+    decode without one (the cluster-merged path). precision: PREC_FFMA (exact F32)
+    or PREC_TF32 (prefill on the tensor cores, head_dim 128)."""
     import torch
     _dev_check(q, k, v)
     Tq, Hq, D = q.shape
@@ -196,9 +210,9 @@ def flash_attn(q, k, v, n_past, scale=0.0, out=None, workspace=None):
     nbytes = lib().b200_flash_attn_workspace_bytes(D, Hq, Hkv, Tq, Tkv)
     if workspace is None:  # zero-filled: the decode split counters start at zero
         workspace = torch.zeros(nbytes, device=q.device, dtype=torch.uint8)
-    _chk("b200_flash_attn", lib().b200_flash_attn(
+    _chk("b200_flash_attn_ex", lib().b200_flash_attn_ex(
         _p(q), _p(k), _p(v), _p(out), D, Hq, Hkv, Tq, Tkv, n_past, scale, Hkv * D, D, Hkv * D, D,
-        _p(workspace), workspace.numel(), _stream()))
+        _p(workspace), workspace.numel(), _stream(), precision))
     return out
 
 

@@ -876,6 +876,10 @@ cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t strea
 
 cudaError_t attn_prefill_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
     if (!strides_ok(a) || a.Tq < 1) return cudaErrorInvalidValue;
+    if (a.precision == 1 && a.D == 128) {  // B200_PREC_TF32
+        const cudaError_t e = attn_prefill_tc_launch(a, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
     switch (a.D) {
         case 64: return pre_by_g<64>(a, stream, pdl);
         case 128: return pre_by_g<128>(a, stream, pdl);

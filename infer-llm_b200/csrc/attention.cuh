@@ -16,6 +16,7 @@ struct AttnArgs {
     int64_t kv_rows = 0;                 // positions the K/V buffers hold (0: n_past + 1)
     const int32_t *n_past_dev = nullptr; // device scalar (graph-replayed decode)
     float scale = 0.f;
+    int precision = 0;                   // B200_PREC_TF32: prefill on the tensor cores (head_dim 128)
     void *ws = nullptr;                  // decode split partials + counters
     size_t ws_bytes = 0;
     int32_t *status = nullptr;
@@ -48,7 +49,11 @@ int attn_decode_splits(int64_t max_len, int64_t Hkv);
 size_t attn_decode_ws_bytes(int64_t D, int64_t Hq, int64_t Hkv, int splits);
 cudaError_t attn_decode_launch(const AttnArgs &a, int splits, cudaStream_t stream, bool pdl);
 
-// Prefill / multi-token (Tq >= 1): tiled online softmax, causal tile skipping.
+// Prefill / multi-token (Tq >= 1): tiled online softmax, causal tile skipping;
+// precision B200_PREC_TF32 with head_dim 128 runs attn_prefill_tc_launch.
 cudaError_t attn_prefill_launch(const AttnArgs &a, cudaStream_t stream, bool pdl);
+// Tensor-core (tcgen05 kind::tf32) prefill, head_dim 128, G = Hq / Hkv in {1, 2, 4, 8};
+// cudaErrorNotSupported where its tensor maps cannot be built.
+cudaError_t attn_prefill_tc_launch(const AttnArgs &a, cudaStream_t stream, bool pdl);
 
 }  // namespace b200

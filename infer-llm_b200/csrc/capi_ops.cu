@@ -1,6 +1,7 @@
 // extern "C" single-op entry points declared in include/b200_infer.h. Each one
 // validates sizes and alignment on the host, then enqueues the sm_100a kernel on
 // the caller's stream. No allocation, no synchronization.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -49,8 +50,20 @@ int b200_device_supported(int device) {
     return p.major == 10 && p.minor == 0 ? 1 : 0;
 }
 
+size_t b200_mul_mat_workspace_bytes(int64_t K, int64_t N, int64_t M, int precision) {
+    if (K <= 0 || N <= 0 || M <= 4) return 0;
+    int64_t f = gemm_ffma_ws_floats(M, N, K);
+    if (precision == B200_PREC_TF32) f = std::max(f, gemm_tf32_ws_floats(M, N, K));
+    return static_cast<size_t>(f) * 4;
+}
+
 int b200_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
                  int precision, void *stream) {
+    return b200_mul_mat_ws(w, x, out, K, N, M, precision, nullptr, 0, stream);
+}
+
+int b200_mul_mat_ws(const float *w, const float *x, float *out, int64_t K, int64_t N, int64_t M,
+                    int precision, void *workspace, size_t workspace_bytes, void *stream) {
     if (K <= 0 || N <= 0 || M < 0) return B200_ERR_INVALID_ARGUMENT;
     if (M == 0) return B200_OK;
     if (!w || !x || !out) return B200_ERR_INVALID_ARGUMENT;
@@ -77,6 +90,10 @@ int b200_mul_mat(const float *w, const float *x, float *out, int64_t K, int64_t 
     g.N = N;
     g.K = K;
     g.epi = GEMM_STORE;
+    if (workspace && !(reinterpret_cast<uintptr_t>(workspace) & 15)) {
+        g.ws = static_cast<float *>(workspace);
+        g.ws_floats = static_cast<int64_t>(workspace_bytes / 4);
+    }
     if (precision == B200_PREC_TF32) {
         const cudaError_t e = gemm_tf32_launch(g, as_stream(stream), false);
         if (e != cudaErrorNotSupported) return from_cuda(e);
@@ -147,10 +164,11 @@ size_t b200_flash_attn_workspace_bytes(int64_t D, int64_t Hq, int64_t Hkv, int64
     return attn_decode_ws_bytes(D, Hq, Hkv, attn_decode_splits(Tkv, Hkv));
 }
 
-int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D, int64_t Hq,
-                    int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past, float scale, int64_t k_tok_stride,
-                    int64_t k_head_stride, int64_t v_tok_stride, int64_t v_head_stride, void *workspace,
-                    size_t workspace_bytes, void *stream) {
+int b200_flash_attn_ex(const float *q, const float *k, const float *v, float *out, int64_t D, int64_t Hq,
+                       int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past, float scale, int64_t k_tok_stride,
+                       int64_t k_head_stride, int64_t v_tok_stride, int64_t v_head_stride, void *workspace,
+                       size_t workspace_bytes, void *stream, int32_t precision) {
+    if (precision != B200_PREC_FFMA && precision != B200_PREC_TF32) return B200_ERR_INVALID_ARGUMENT;
     if (!q || !k || !v || !out || D <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Tq < 0 || n_past < 0)
         return B200_ERR_INVALID_ARGUMENT;
     if (Tkv != n_past + Tq) return B200_ERR_INVALID_ARGUMENT;
@@ -170,6 +188,7 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
     a.Tq = Tq;
     a.n_past = n_past;
     a.scale = scale;
+    a.precision = precision;
     a.ws = workspace;
     a.ws_bytes = workspace_bytes;
     cudaStream_t st = as_stream(stream);
@@ -181,6 +200,14 @@ int b200_flash_attn(const float *q, const float *k, const float *v, float *out, 
         return from_cuda(attn_decode_launch(a, S, st, false));
     }
     return from_cuda(attn_prefill_launch(a, st, false));
+}
+
+int b200_flash_attn(const float *q, const float *k, const float *v, float *out, int64_t D, int64_t Hq,
+                    int64_t Hkv, int64_t Tq, int64_t Tkv, int64_t n_past, float scale, int64_t k_tok_stride,
+                    int64_t k_head_stride, int64_t v_tok_stride, int64_t v_head_stride, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    return b200_flash_attn_ex(q, k, v, out, D, Hq, Hkv, Tq, Tkv, n_past, scale, k_tok_stride, k_head_stride,
+                              v_tok_stride, v_head_stride, workspace, workspace_bytes, stream, B200_PREC_FFMA);
 }
 
 int b200_silu(const float *x, float *out, int64_t n, void *stream) {

@@ -302,6 +302,7 @@ int enqueue_small_step(b200_engine *e, const int32_t *first_ids, int M, bool wan
             a.early_kv = pdl;  // the QKV GEMV before it signals late (late_launch)
             B200_TRY(mark(e, "attn_decode", attn_decode_launch(a, e->attn_splits, st, pdl)));
         } else {
+            a.precision = e->c.precision;
             B200_TRY(mark(e, "attn_prefill", attn_prefill_launch(a, st, pdl)));
         }
 
@@ -449,6 +450,8 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         a.Hkv = e->Hkv;
         a.Tq = n;
         a.n_past_dev = e->n_past_dev;
+        a.kv_rows = e->c.kv_capacity;
+        a.precision = e->c.precision;
         a.status = e->status;
         B200_TRY(attn_prefill_launch(a, st, pdl));
 

@@ -38,6 +38,10 @@ cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl);
 // Sums a.ws[0..splits) (split-K partials, [M][N] each) in split order and applies
 // a.epi into a.c.
 cudaError_t gemm_splitk_reduce_launch(const GemmArgs &a, int splits, cudaStream_t stream, bool pdl);
+// Split-K workspace (floats) that lets each GEMM use all its splits at M x N x K
+// (0: no split at this shape).
+int64_t gemm_ffma_ws_floats(int64_t M, int64_t N, int64_t K);
+int64_t gemm_tf32_ws_floats(int64_t M, int64_t N, int64_t K);
 int device_sm_count();
 
 }  // namespace b200

@@ -215,16 +215,24 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
     }
 }
 
+// K splits for an M x N x K product with BM-row tiles: when the tile grid leaves
+// SMs idle (prompts up to a few hundred tokens on the layer shapes), about two CTAs
+// per SM, at least 128 of K (8 k-steps) per split.
+template <int BM>
+int64_t ffma_splits(int64_t M, int64_t N, int64_t K) {
+    const int64_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM), target = 2 * device_sm_count();
+    if (tiles >= target || K < 256) return 1;
+    return std::max<int64_t>(1, std::min<int64_t>((target + tiles - 1) / tiles, K / 128));
+}
+
 template <int BM>
 cudaError_t launch_bm(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
     GemmArgs a = a_in;
     dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + BM - 1) / BM));
-    // Split K when the tile grid leaves most SMs idle (decode-sized prompts): aim
-    // for about two CTAs per SM, at least 256 of K per split, partials in a.ws.
+    // split K (partials in a.ws, reduced in split order) when the tiles leave SMs idle
     a.k_split = 0;
-    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y, target = 2 * device_sm_count();
-    if (a.ws && tiles < target && a.K >= 512) {
-        int64_t splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
+    if (a.ws) {
+        int64_t splits = ffma_splits<BM>(a.M, a.N, a.K);
         while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
         if (splits > 1) {
             a.k_split = ((a.K + splits - 1) / splits + BK - 1) / BK * BK;
@@ -256,6 +264,12 @@ cudaError_t gemm_splitk_reduce_launch(const GemmArgs &a, int splits, cudaStream_
         case GEMM_SWIGLU: return b200_launch(splitk_reduce_kernel<GEMM_SWIGLU>, rg, dim3(256), 0, stream, pdl, a, splits);
     }
     return cudaErrorInvalidValue;
+}
+
+int64_t gemm_ffma_ws_floats(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const int64_t s = M <= 32 ? ffma_splits<32>(M, N, K) : M <= 64 ? ffma_splits<64>(M, N, K) : ffma_splits<128>(M, N, K);
+    return s > 1 ? s * M * N : 0;
 }
 
 cudaError_t gemm_ffma_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {

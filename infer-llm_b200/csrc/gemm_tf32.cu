@@ -28,6 +28,7 @@
 #include <algorithm>
 
 #include "gemm.cuh"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace b200 {
@@ -48,26 +49,9 @@ struct TCfg {
     static constexpr uint32_t kAccCols = BN;            // one F32 accumulator: 128 lanes x BN columns
     static constexpr uint32_t kTmemCols = 2 * BN;       // two, so a tile's epilogue overlaps the next tile's MMAs
     static constexpr size_t kSmem = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes + 256;
-    // Instruction descriptor of kind::tf32: F32 accumulate (bits 4-5 = 1), A and B
-    // TF32 (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bits
-    // 17-22, M >> 4 at bits 24-28.
-    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                                       (static_cast<uint32_t>(kTBM >> 4) << 24);
+    // kind::tf32, both operands K-major
+    static constexpr uint32_t kIdesc = idesc_tf32(kTBM, BN, false, false);
 };
-
-// Shared-memory matrix descriptor for a K-major tile written by TMA with the
-// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte
-// offset), leading byte offset unused (1), descriptor version 1, layout SWIZZLE_128B
-// (2 at bits 61-63). The tile base is 1024-byte aligned; stepping K by 8 TF32
-// elements inside the 128-byte row advances the start address by 32 bytes.
-B200_DEVICE uint64_t desc_k_sw128(uint32_t saddr) {
-    uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>(1) << 16;
-    d |= static_cast<uint64_t>(1024 >> 4) << 32;
-    d |= static_cast<uint64_t>(1) << 46;
-    d |= static_cast<uint64_t>(2) << 61;
-    return d;
-}
 
 B200_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y, uint32_t bar) {
     asm volatile(
@@ -75,54 +59,6 @@ B200_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, in
             "r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
-}
-
-B200_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-B200_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-B200_DEVICE void tc_mma_tf32(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem),
-        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
-}
-
-// Arrives on `bar` once every tcgen05.mma this thread issued so far has completed.
-B200_DEVICE void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-
-// 32 lanes x 16 consecutive 32-bit columns of tensor memory (thread t: lane t).
-B200_DEVICE void tc_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-// Bounded mbarrier wait (hardware-suspended polls); false and B200_DEV_TIMEOUT
-// after ~2 s, or at once if another CTA already reported an error.
-B200_DEVICE bool wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-#pragma unroll 1
-    for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-        if ((i & 7) == 7) {
-            if (status && *reinterpret_cast<volatile int32_t *>(status)) return false;
-            if (global_ns() - t0 > 2000000000ull) break;
-        }
-    }
-    set_status(status, B200_DEV_TIMEOUT);
-    return false;
 }
 
 __device__ int32_t g_tf32_status;  // status word when the caller passes none
@@ -359,6 +295,15 @@ cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmA
     return b200_launch(gemm_tf32_kernel<EPI, BN>, grid, dim3(kTThreads), TCfg<BN>::kSmem, st, pdl, mx, mw, a, n_tiles);
 }
 
+// K splits of the tcgen05 GEMM with BN-wide tiles: about one tile per SM, at least
+// 256 of K per split, when the tile grid alone leaves SMs idle.
+template <int BN>
+int64_t tf32_splits(int64_t M, int64_t N, int64_t K) {
+    const int64_t tiles = ((N + BN - 1) / BN) * ((M + kTBM - 1) / kTBM), target = device_sm_count();
+    if (tiles >= target || K < 512) return 1;
+    return std::max<int64_t>(1, std::min<int64_t>((target + tiles - 1) / tiles, K / 256));
+}
+
 template <int BN>
 cudaError_t launch_bn(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
     GemmArgs a = a_in;
@@ -369,9 +314,8 @@ cudaError_t launch_bn(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
     // SM, at least 256 of K per split, partials reduced in split order.
     a.k_split = 0;
     int64_t splits = 1;
-    const int64_t target = device_sm_count();
-    if (a.ws && tiles < target && a.K >= 512) {
-        splits = std::min<int64_t>((target + tiles - 1) / tiles, a.K / 256);
+    if (a.ws) {
+        splits = tf32_splits<BN>(a.M, a.N, a.K);
         while (splits > 1 && splits * a.M * a.N > a.ws_floats) --splits;
         if (splits > 1) {
             a.k_split = ((a.K + splits - 1) / splits + kTBK - 1) / kTBK * kTBK;
@@ -395,6 +339,13 @@ cudaError_t launch_bn(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
 }
 
 }  // namespace
+
+int64_t gemm_tf32_ws_floats(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const int64_t tiles256 = ((N + 255) / 256) * ((M + kTBM - 1) / kTBM);
+    const int64_t s = tiles256 >= device_sm_count() ? tf32_splits<256>(M, N, K) : tf32_splits<128>(M, N, K);
+    return s > 1 ? s * M * N : 0;
+}
 
 cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaErrorInvalidValue;

@@ -53,6 +53,26 @@ constexpr int kMaxDevices = 64;
 AttnWorkspace g_attn_ws[kMaxDevices];
 std::mutex g_attn_ws_mu;
 
+// The prefill GEMM's split-K partials, one grow-only buffer per device (contents
+// need no initialisation: every split writes its whole partial tile).
+struct GemmWorkspace {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+GemmWorkspace g_gemm_ws[kMaxDevices];
+std::mutex g_gemm_ws_mu;
+
+// Device that holds `p` (device memory only), or -1.
+int device_of(const void *p) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, p) != cudaSuccess || pa.type != cudaMemoryTypeDevice || pa.device < 0 ||
+        pa.device >= kMaxDevices) {
+        cudaGetLastError();
+        return -1;
+    }
+    return pa.device;
+}
+
 // Restores the current device on scope exit.
 struct CurrentDevice {
     int prev = -1;
@@ -74,7 +94,24 @@ cudaError_t compute_mul_mat(Tensor *dst, cudaStream_t s) {
     const Tensor *w = dst->src[0], *x = dst->src[1];
     if (w->dims[0] != x->dims[0] || w->dims[1] != dst->dims[0] || x->dims[1] != dst->dims[1])
         return cudaErrorInvalidValue;
-    return as_cuda(b200_mul_mat(cf(w), cf(x), mf(dst), w->dims[0], w->dims[1], x->dims[1], B200_PREC_FFMA, s));
+    const int64_t K = w->dims[0], N = w->dims[1], M = x->dims[1];
+    const size_t need = b200_mul_mat_workspace_bytes(K, N, M, B200_PREC_FFMA);
+    if (need == 0) return as_cuda(b200_mul_mat(cf(w), cf(x), mf(dst), K, N, M, B200_PREC_FFMA, s));
+    // prompts of a few hundred tokens: split K across the SMs through the workspace
+    // of the device that holds x
+    const int dev = device_of(x->data);
+    if (dev < 0) return cudaErrorInvalidValue;
+    CurrentDevice on(dev);
+    std::lock_guard<std::mutex> lock(g_gemm_ws_mu);
+    GemmWorkspace &ws = g_gemm_ws[dev];
+    if (need > ws.bytes) {
+        if (ws.ptr && cudaFree(ws.ptr) != cudaSuccess) return cudaErrorUnknown;
+        ws.ptr = nullptr;
+        ws.bytes = 0;
+        if (cudaMalloc(&ws.ptr, need) != cudaSuccess) return cudaErrorMemoryAllocation;
+        ws.bytes = need;
+    }
+    return as_cuda(b200_mul_mat_ws(cf(w), cf(x), mf(dst), K, N, M, B200_PREC_FFMA, ws.ptr, ws.bytes, s));
 }
 
 cudaError_t compute_rms_norm(Tensor *dst, cudaStream_t s) {
@@ -99,15 +136,11 @@ cudaError_t compute_flash_attn(Tensor *dst, cudaStream_t s) {
     // Decode splits merge through a zero-filled workspace that later calls reuse; it
     // grows with the context (the reference kernel mallocs a score matrix per call,
     // kernel_f32.cu:484-510). The workspace is the one of the device that holds q.
-    cudaPointerAttributes pa{};
-    if (cudaPointerGetAttributes(&pa, q->data) != cudaSuccess || pa.type != cudaMemoryTypeDevice ||
-        pa.device < 0 || pa.device >= kMaxDevices) {
-        cudaGetLastError();
-        return cudaErrorInvalidValue;
-    }
-    CurrentDevice on(pa.device);
+    const int dev = device_of(q->data);
+    if (dev < 0) return cudaErrorInvalidValue;
+    CurrentDevice on(dev);
     std::lock_guard<std::mutex> lock(g_attn_ws_mu);
-    AttnWorkspace &ws = g_attn_ws[pa.device];
+    AttnWorkspace &ws = g_attn_ws[dev];
     const size_t need = b200_flash_attn_workspace_bytes(D, q->dims[1], k->dims[1], q->dims[2], k->dims[2]);
     if (need > ws.bytes) {
         if (ws.ptr && cudaFree(ws.ptr) != cudaSuccess) return cudaErrorUnknown;

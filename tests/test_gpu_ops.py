@@ -161,7 +161,9 @@ def test_flash_attn_prefill(cuda, port, S):
 
 
 @pytest.mark.parametrize("Tq,n_past,Hq,Hkv,D", [(40, 100, 16, 8, 128), (3, 5, 16, 8, 128), (65, 0, 4, 4, 64),
-                                                 (17, 9, 32, 8, 128), (9, 30, 8, 1, 64)])
+                                                 (17, 9, 32, 8, 128), (9, 30, 8, 1, 64),
+                                                 (33, 0, 8, 1, 128), (130, 7, 8, 8, 128), (200, 77, 16, 8, 128),
+                                                 (257, 0, 32, 8, 128)])
 def test_flash_attn_chunked_and_gqa(cuda, port, Tq, n_past, Hq, Hkv, D):
     rng = np.random.default_rng(Tq + n_past)
     q, k, v = _attn_case(rng, Tq, n_past, Hq, Hkv, D)

@@ -1,4 +1,4 @@
-"""The tcgen05 TF32 prefill GEMM (B200_PREC_TF32) and the engine on it.
+"""The tcgen05 TF32 prefill GEMM and attention (B200_PREC_TF32) and the engine on them.
 
 Op level: C = X . W^T through b200_mul_mat with precision TF32, against
   (1) the product of the TF32-rounded operands in float64: the tensor cores read
@@ -87,6 +87,77 @@ def test_tf32_engine_matches_golden(cuda, golden, tmp_path):
     eng.eval(np.array([3, 4, 5, 6, 7, 8, 9], np.int32), logits)
     assert np.all(np.isfinite(logits))
     eng.close()
+
+
+def attn_f64(q, k, v, n_past, scale, tc):
+    """Causal GQA attention in float64 on the device; q (Tq, Hq, D), k / v (Tkv, Hkv, D).
+
+    tc: the tensor-core computation's roundings: Q, K, V and the probabilities P
+    rounded to the nearest TF32 value (top 19 bits, ties away from zero), P
+    normalised by the sum of its rounded values."""
+    def f(a):
+        a = a.contiguous()
+        if tc:
+            a = ((a.view(torch.int32) + 0x1000) & -8192).view(torch.float32)
+        return a.double()
+    Tq, Hq, D = q.shape
+    Tkv, Hkv, _ = k.shape
+    g = Hq // Hkv
+    kk = f(k).repeat_interleave(g, dim=1)
+    vv = f(v).repeat_interleave(g, dim=1)
+    s = torch.einsum("qhd,khd->hqk", f(q), kk) * scale
+    mask = torch.arange(Tkv, device=q.device)[None, :] > (n_past + torch.arange(Tq, device=q.device))[:, None]
+    s = s.masked_fill(mask[None], float("-inf"))
+    p = torch.exp(s - s.amax(-1, keepdim=True))
+    if tc:
+        p = ((p.float().view(torch.int32) + 0x1000) & -8192).view(torch.float32).double()
+    return torch.einsum("hqk,khd->qhd", p / p.sum(-1, keepdim=True), vv).cpu().numpy()
+
+
+def err_v(got, want, v):
+    """max |got - want| / RMS(V): an attention output is a convex combination of V
+    rows, so V's scale is the natural unit of its error at any context length."""
+    v = v.double()
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / float(torch.sqrt(torch.mean(v * v))))
+
+
+ATTN_CASES = [  # (Tq, n_past, Hq, Hkv): prefill, chunked prefill, GQA group sizes
+    (64, 0, 16, 8), (200, 0, 16, 8), (2048, 0, 16, 8), (37, 90, 16, 8), (130, 7, 8, 8),
+    (257, 0, 32, 8), (33, 300, 8, 1), (1, 40, 16, 8), (512, 1500, 32, 8),
+]
+
+
+@pytest.mark.parametrize("Tq,n_past,Hq,Hkv", ATTN_CASES)
+def test_flash_attn_tf32(cuda, Tq, n_past, Hq, Hkv):
+    """Prefill attention with precision TF32 (S = Q K^T and O = P V on the tensor
+    cores, head_dim 128) against float64 attention: (1) the same roundings emulated
+    (Q, K, V and P rounded to the nearest TF32 value, P normalised by its rounded
+    sum): within 5e-4 of V's RMS (what remains is F32 accumulation order
+    and P rounded at the kernel's running row max); (2) exact attention: within the
+    emulation's own error plus 5e-4 of V's RMS, and within 4e-3 of V's RMS (the
+    stated op-level TF32 bound). Exact FFMA attention on the same inputs stays within
+    1e-5 (rel_err); Tq = 1 is decode, which is exact in either precision."""
+    D = 128
+    g = torch.Generator(device=cuda).manual_seed(Tq * 7 + n_past)
+    L = n_past + Tq
+    q = torch.randn((Tq, Hq, D), device=cuda, generator=g)
+    k = torch.randn((L, Hkv, D), device=cuda, generator=g)
+    v = torch.randn((L, Hkv, D), device=cuda, generator=g)
+    got = B.flash_attn(q, k, v, n_past, precision=B.PREC_TF32).cpu().numpy()
+    scale = 1.0 / np.sqrt(D)
+    exact = attn_f64(q, k, v, n_past, scale, False)
+    emul = attn_f64(q, k, v, n_past, scale, True)
+    e_emul, e_exact, e_model = err_v(got, emul, v), err_v(got, exact, v), err_v(emul, exact, v)
+    print(f"tf32 attention Tq={Tq} n_past={n_past} G={Hq // Hkv} (x RMS(V)): vs emulated {e_emul:.2e}, "
+          f"vs exact {e_exact:.2e} (emulated vs exact {e_model:.2e}); rel_err vs exact {rel_err(got, exact):.2e}")
+    if Tq == 1:
+        assert rel_err(got, exact) <= 1e-5
+    else:
+        assert e_emul <= 5e-4
+        assert e_exact <= e_model + 5e-4
+        assert e_exact <= 4e-3
+    ffma = B.flash_attn(q, k, v, n_past).cpu().numpy()
+    assert rel_err(ffma, exact) <= 1e-5
 
 
 @pytest.mark.parametrize("plen", [32, 160])

@@ -192,6 +192,8 @@ def _leaving_worker(rank, world, port, mode, out):
         out.put(("completed", time.monotonic() - t0))
     except Exception as e:  # gloo reports the lost peer / the timeout
         out.put((type(e).__name__, time.monotonic() - t0))
+    out.close()
+    out.join_thread()  # the queue's feeder thread has sent the result before the hard exit
     os._exit(0)
 
 
