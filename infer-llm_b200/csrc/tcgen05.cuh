@@ -140,4 +140,22 @@ B200_DEVICE bool wait_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
     return false;
 }
 
+// As wait_bounded, with plain try_wait polls and no suspend-time hint: the thread
+// resumes as soon as the phase completes (a hinted wait may let a thread sleep ~1 µs
+// past the completion, which a per-tile handshake on the critical path cannot afford).
+B200_DEVICE bool wait_poll(uint64_t *bar, uint32_t parity, int32_t *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+#pragma unroll 1
+    for (uint32_t i = 0; i < B200_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 255) {
+            if (status && *reinterpret_cast<volatile int32_t *>(status)) return false;
+            if (global_ns() - t0 > 2000000000ull) break;
+        }
+    }
+    set_status(status, B200_DEV_TIMEOUT);
+    return false;
+}
+
 }  // namespace b200
