@@ -590,8 +590,11 @@ __global__ void __launch_bounds__(kPreThreads, 1) attn_prefill_kernel(const Attn
     grid_wait();
 
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int64_t qb = gridDim.x - 1 - blockIdx.x;  // heaviest blocks first
-    const int64_t kvh = blockIdx.y;
+    // one CTA per (query block, KV head), the heaviest query blocks (most keys under
+    // the causal mask) of every head first: the first wave takes the longest CTAs
+    const int64_t nqb = gridDim.x / a.Hkv;
+    const int64_t qb = nqb - 1 - blockIdx.x / a.Hkv;
+    const int64_t kvh = blockIdx.x % a.Hkv;
     const int64_t q0 = qb * BQ;
     const int64_t n_past = a.n_past_dev ? static_cast<int64_t>(*a.n_past_dev) : a.n_past;
     const int64_t Tkv = n_past + a.Tq;
@@ -805,7 +808,7 @@ cudaError_t pre_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
         });
         if (e != cudaSuccess) return e;
     }
-    const dim3 grid(static_cast<unsigned>((a.Tq + BQ - 1) / BQ), static_cast<unsigned>(a.Hkv));
+    const dim3 grid(static_cast<unsigned>(((a.Tq + BQ - 1) / BQ) * a.Hkv));
     return b200_launch(kern, grid, dim3(kPreThreads), smem, stream, pdl, a);
 }
 

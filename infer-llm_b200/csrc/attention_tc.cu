@@ -38,7 +38,8 @@
 // zeroed in shared memory (the cache may hold anything there; 0 x NaN is NaN).
 // Numerics: TF32 products of operands rounded to nearest, F32 accumulation; on
 // N(0, 1) inputs the output moves from exact attention by ~1e-3 of V's RMS, without
-// the truncation bias.
+// the truncation bias. The output is written rounded to the nearest TF32 value: in
+// the B200_PREC_TF32 layer it feeds the o_proj product only.
 //
 // Every mbarrier wait is bounded (wait_poll, tcgen05.cuh): a wait that runs out records
 // B200_DEV_TIMEOUT in the status word; the CTA then waits (bounded) for its copies
@@ -137,8 +138,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int32_t *status = a.status ? a.status : &g_attn_tc_status;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t qb = gridDim.x - 1 - blockIdx.x;  // heaviest blocks first
-    const int64_t kvh = blockIdx.y;
+    // one CTA per (query block, KV head), the heaviest query blocks (most keys under
+    // the causal mask) of every head first: the first wave takes the longest CTAs
+    const int64_t nqb = gridDim.x / a.Hkv;
+    const int64_t qb = nqb - 1 - blockIdx.x / a.Hkv;
+    const int64_t kvh = blockIdx.x % a.Hkv;
     const int64_t q0 = qb * BQ;
 
     if (threadIdx.x == 0) {
@@ -409,8 +413,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                     for (int c = 0; c < 32; c += 4)
                         *reinterpret_cast<float4 *>(dst + 32 * cb + c) =
-                            make_float4(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv,
-                                        __uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
+                            make_float4(tf32_rn(__uint_as_float(o[c]) * inv), tf32_rn(__uint_as_float(o[c + 1]) * inv),
+                                        tf32_rn(__uint_as_float(o[c + 2]) * inv), tf32_rn(__uint_as_float(o[c + 3]) * inv));
                 }
             }
         }
@@ -451,7 +455,7 @@ cudaError_t tc_launch(const AttnArgs &a, cudaStream_t stream, bool pdl) {
         !kv_map(&mv, a.v, a.Hkv, rows, a.v_head, a.v_tok, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
         return cudaErrorNotSupported;
     constexpr int BQ = kTcRows / G;
-    const dim3 grid(static_cast<unsigned>((a.Tq + BQ - 1) / BQ), static_cast<unsigned>(a.Hkv));
+    const dim3 grid(static_cast<unsigned>(((a.Tq + BQ - 1) / BQ) * a.Hkv));
     return b200_launch(kern, grid, dim3(kTcThreads), kTcSmem, stream, pdl, mk, mv, a);
 }
 

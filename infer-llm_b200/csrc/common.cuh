@@ -158,6 +158,11 @@ B200_DEVICE void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, 
         : "memory");
 }
 
+// Nearest TF32 value of x (top 19 bits, ties away from zero). Kernels whose output
+// only feeds a TF32 tensor-core product write it rounded: the tensor cores would
+// truncate it, a bias toward zero that compounds over the layers.
+B200_DEVICE float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+
 B200_DEVICE uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

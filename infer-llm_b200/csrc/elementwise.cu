@@ -17,7 +17,7 @@ namespace {
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x,
                                                        const float *__restrict__ gamma,
                                                        float *__restrict__ out, int64_t D,
-                                                       int64_t rows, float eps) {
+                                                       int64_t rows, float eps, bool round_tf32) {
     grid_launch_dependents();
     grid_wait();
     const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -33,7 +33,10 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__
     }
     ss = warp_sum(ss);
     const float sc = rms_scale_from_sumsq(ss, D, eps);
-    for (int64_t k = lane; k < D; k += 32) yr[k] = __fmul_rn(__fmul_rn(xr[k], sc), gamma[k]);
+    for (int64_t k = lane; k < D; k += 32) {
+        const float y = __fmul_rn(__fmul_rn(xr[k], sc), gamma[k]);
+        yr[k] = round_tf32 ? tf32_rn(y) : y;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -247,10 +250,10 @@ unsigned grid_for(int64_t items, int per_block) {
 }  // namespace
 
 cudaError_t rms_norm_launch(const float *x, const float *gamma, float *out, int64_t D, int64_t rows,
-                            float eps, cudaStream_t stream, bool pdl) {
+                            float eps, cudaStream_t stream, bool pdl, bool round_tf32) {
     if (rows == 0) return cudaSuccess;
     return b200_launch(rms_norm_kernel, dim3(grid_for(rows, 8)), dim3(256), 0, stream, pdl, x, gamma,
-                       out, D, rows, eps);
+                       out, D, rows, eps, round_tf32);
 }
 
 cudaError_t rope_table_launch(const float *x, const int32_t *pos, const float *table, int64_t n_ctx,

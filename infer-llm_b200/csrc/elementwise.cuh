@@ -5,8 +5,9 @@
 
 namespace b200 {
 
+// round_tf32: outputs rounded to the nearest TF32 value (they feed a TF32 product)
 cudaError_t rms_norm_launch(const float *x, const float *gamma, float *out, int64_t D, int64_t rows,
-                            float eps, cudaStream_t stream, bool pdl);
+                            float eps, cudaStream_t stream, bool pdl, bool round_tf32 = false);
 
 cudaError_t rope_table_launch(const float *x, const int32_t *pos, const float *table, int64_t n_ctx,
                               float *out, int64_t D, int64_t H, int64_t T, int32_t *status,

@@ -394,7 +394,9 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
     B200_TRY(get_rows_launch(e->tok_embd, e->ids, e->x, H, n, e->c.n_vocab, e->status, st, pdl));
     for (int l = 0; l < e->c.n_layer; ++l) {
         const LayerW &w = e->L[l];
-        B200_TRY(rms_norm_launch(e->x, w.attn_norm, e->xn, H, n, e->c.rms_eps, st, pdl));
+        // TF32: the normalised rows only feed TF32 products, written rounded to nearest
+        const bool tf32 = e->c.precision == B200_PREC_TF32;
+        B200_TRY(rms_norm_launch(e->x, w.attn_norm, e->xn, H, n, e->c.rms_eps, st, pdl, tf32));
         GemmArgs g;
         g.x = e->xn;
         g.ldx = H;
@@ -472,7 +474,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         B200_TRY(e->c.precision == B200_PREC_TF32 ? gemm_tf32_launch(o, st, pdl) : gemm_ffma_launch(o, st, pdl));
         if (e->tp) B200_TRY(tp_allreduce(e->tp, e->x, static_cast<size_t>(n) * H, st, false, e->status));
 
-        B200_TRY(rms_norm_launch(e->x, w.ffn_norm, e->xn, H, n, e->c.rms_eps, st, pdl));
+        B200_TRY(rms_norm_launch(e->x, w.ffn_norm, e->xn, H, n, e->c.rms_eps, st, pdl, tf32));
         GemmArgs gu;
         gu.x = e->xn;
         gu.ldx = H;
@@ -483,6 +485,7 @@ int enqueue_prefill(b200_engine *e, int n, bool want_logits) {
         gu.N = 2 * static_cast<int64_t>(e->F);
         gu.K = H;
         gu.epi = GEMM_SWIGLU;
+        gu.round_out = tf32;  // h feeds the down product only
         gu.ws = e->gemm_ws;
         gu.ws_floats = e->gemm_ws_floats;
         gu.status = e->status;

@@ -27,6 +27,9 @@ struct GemmArgs {
     int64_t ws_floats = 0;
     int64_t k_split = 0;  // set by the launcher: K per split (0 = no split)
     int32_t *status = nullptr;  // device status word for bounded-wait timeouts (tcgen05 GEMM)
+    // Outputs rounded to the nearest TF32 value (they only feed a later TF32 product;
+    // honoured by the tcgen05 GEMM and the split-K reduction).
+    bool round_out = false;
 };
 
 // Exact F32 FFMA tiled GEMM (any M; K % 4 == 0).

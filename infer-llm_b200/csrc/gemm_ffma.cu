@@ -15,8 +15,10 @@ namespace {
 
 constexpr int BN = 128, BK = 16, PAD = 4, NT = 256;
 
+// Two CTAs per SM (at most 128 registers a thread): 16 warps to hide the shared-memory
+// and FFMA latencies, and the split-K grid below is sized for two CTAs per SM.
 template <int BM, int EPI>
-__global__ void __launch_bounds__(NT) sgemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(NT, 2) sgemm_kernel(const GemmArgs a) {
     constexpr int TM = BM / 16;              // rows per thread
     constexpr int A_LD = (BM * BK / 4) / NT; // float4 loads of X per thread (BM=32 -> 0.5)
     __shared__ __align__(16) float As[2][BK][BM + PAD];
@@ -206,23 +208,24 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
             u += a.ws[z * plane + m * a.N + 2 * n + 1];
         }
         const float sg = g / (1.0f + expf(-g));
-        a.c[m * a.ldc + n] = u * sg;
+        a.c[m * a.ldc + n] = a.round_out ? tf32_rn(u * sg) : u * sg;
     } else {
         float v = 0.f;
         for (int z = 0; z < splits; ++z) v += a.ws[z * plane + m * a.N + n];
         if (EPI == GEMM_RESIDUAL) v = v + a.r[m * a.ldc + n];
-        a.c[m * a.ldc + n] = v;
+        a.c[m * a.ldc + n] = a.round_out ? tf32_rn(v) : v;
     }
 }
 
 // K splits for an M x N x K product with BM-row tiles: when the tile grid leaves
-// SMs idle (prompts up to a few hundred tokens on the layer shapes), about two CTAs
-// per SM, at least 128 of K (8 k-steps) per split.
+// SMs idle (prompts up to a few hundred tokens on the layer shapes), as many splits
+// as fit in one wave of two CTAs per SM (a partial second wave would double the
+// time), at least 128 of K (8 k-steps) per split.
 template <int BM>
 int64_t ffma_splits(int64_t M, int64_t N, int64_t K) {
     const int64_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM), target = 2 * device_sm_count();
     if (tiles >= target || K < 256) return 1;
-    return std::max<int64_t>(1, std::min<int64_t>((target + tiles - 1) / tiles, K / 128));
+    return std::max<int64_t>(1, std::min<int64_t>(target / tiles, K / 128));
 }
 
 template <int BM>

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     for (int i = 0; i < 8; ++i) {
                         const float g = v[2 * i], u = v[2 * i + 1];
                         const float sg = g / (1.0f + expf(-g));
-                        h[i] = u * sg;
+                        h[i] = a.round_out ? tf32_rn(u * sg) : u * sg;
                     }
                     float *dst = a.c + gm * a.ldc + gn / 2;
                     if (whole && vec_c) {
@@ -249,6 +249,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
                             if (gn + i < a.N) v[i] = v[i] + res[i];
+                    }
+                    if (a.round_out) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] = tf32_rn(v[i]);
                     }
                     if (whole && vec_c) {
 #pragma unroll
@@ -295,13 +299,14 @@ cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmA
     return b200_launch(gemm_tf32_kernel<EPI, BN>, grid, dim3(kTThreads), TCfg<BN>::kSmem, st, pdl, mx, mw, a, n_tiles);
 }
 
-// K splits of the tcgen05 GEMM with BN-wide tiles: about one tile per SM, at least
-// 256 of K per split, when the tile grid alone leaves SMs idle.
+// K splits of the tcgen05 GEMM with BN-wide tiles, when the tile grid alone leaves
+// SMs idle: as many as fit in one round of the persistent grid (one tile per SM; a
+// partial second round would double the time), at least 256 of K per split.
 template <int BN>
 int64_t tf32_splits(int64_t M, int64_t N, int64_t K) {
     const int64_t tiles = ((N + BN - 1) / BN) * ((M + kTBM - 1) / kTBM), target = device_sm_count();
     if (tiles >= target || K < 512) return 1;
-    return std::max<int64_t>(1, std::min<int64_t>((target + tiles - 1) / tiles, K / 256));
+    return std::max<int64_t>(1, std::min<int64_t>(target / tiles, K / 256));
 }
 
 template <int BN>

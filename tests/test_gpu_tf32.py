@@ -94,7 +94,8 @@ def attn_f64(q, k, v, n_past, scale, tc):
 
     tc: the tensor-core computation's roundings: Q, K, V and the probabilities P
     rounded to the nearest TF32 value (top 19 bits, ties away from zero), P
-    normalised by the sum of its rounded values."""
+    normalised by the sum of its rounded values. (The kernel also writes its output
+    rounded to TF32; the comparison allows that half-ulp separately.)"""
     def f(a):
         a = a.contiguous()
         if tc:
@@ -114,11 +115,16 @@ def attn_f64(q, k, v, n_past, scale, tc):
     return torch.einsum("hqk,khd->qhd", p / p.sum(-1, keepdim=True), vv).cpu().numpy()
 
 
-def err_v(got, want, v):
+def err_v(got, want, v, out_half_ulp=False):
     """max |got - want| / RMS(V): an attention output is a convex combination of V
-    rows, so V's scale is the natural unit of its error at any context length."""
+    rows, so V's scale is the natural unit of its error at any context length.
+    out_half_ulp: first take off, per element, the half TF32 ulp (2^-11 |want|) by
+    which rounding the output to TF32 may move it."""
     v = v.double()
-    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / float(torch.sqrt(torch.mean(v * v))))
+    d = np.abs(np.asarray(got, np.float64) - want)
+    if out_half_ulp:
+        d = np.maximum(d - 2.0 ** -11 * np.abs(want), 0.0)
+    return float(np.max(d) / float(torch.sqrt(torch.mean(v * v))))
 
 
 ATTN_CASES = [  # (Tq, n_past, Hq, Hkv): prefill, chunked prefill, GQA group sizes
@@ -132,7 +138,8 @@ def test_flash_attn_tf32(cuda, Tq, n_past, Hq, Hkv):
     """Prefill attention with precision TF32 (S = Q K^T and O = P V on the tensor
     cores, head_dim 128) against float64 attention: (1) the same roundings emulated
     (Q, K, V and P rounded to the nearest TF32 value, P normalised by its rounded
-    sum): within 5e-4 of V's RMS (what remains is F32 accumulation order
+    sum): within 5e-4 of V's RMS beyond the half TF32 ulp of the rounded output
+    (that allowance applies to (2) as well) (what remains is F32 accumulation order
     and P rounded at the kernel's running row max); (2) exact attention: within the
     emulation's own error plus 5e-4 of V's RMS, and within 4e-3 of V's RMS (the
     stated op-level TF32 bound). Exact FFMA attention on the same inputs stays within
@@ -147,7 +154,7 @@ def test_flash_attn_tf32(cuda, Tq, n_past, Hq, Hkv):
     scale = 1.0 / np.sqrt(D)
     exact = attn_f64(q, k, v, n_past, scale, False)
     emul = attn_f64(q, k, v, n_past, scale, True)
-    e_emul, e_exact, e_model = err_v(got, emul, v), err_v(got, exact, v), err_v(emul, exact, v)
+    e_emul, e_exact, e_model = err_v(got, emul, v, True), err_v(got, exact, v, True), err_v(emul, exact, v)
     print(f"tf32 attention Tq={Tq} n_past={n_past} G={Hq // Hkv} (x RMS(V)): vs emulated {e_emul:.2e}, "
           f"vs exact {e_exact:.2e} (emulated vs exact {e_model:.2e}); rel_err vs exact {rel_err(got, exact):.2e}")
     if Tq == 1:
