@@ -35,19 +35,25 @@ namespace b200 {
 namespace {
 
 constexpr int kTBM = 128, kTBK = 32;  // kTBK floats = one 128-byte swizzle row
-constexpr uint32_t kTileA = kTBM * kTBK * 4;  // 16 KB of X per stage
-constexpr int kEpiWarps = 4;                   // warps 2..5: TMEM lane quarters (warp % 4) 2, 3, 0, 1
+constexpr int kEpiWarps = 4;           // warps 2..5: TMEM lane quarters (warp % 4) 2, 3, 0, 1
 constexpr int kTThreads = 32 * (2 + kEpiWarps);
 
 // Tile width BN (output features per tile): 256 when the tiles fill the SMs, else 128.
-template <int BN>
+// MB: 128-row halves per tile. MB = 1: 128 x BN tiles, two accumulators so a tile's
+// epilogue overlaps the next tile's MMAs. MB = 2 (BN 256): 256 x 256 tiles, the two
+// accumulators hold the two row halves of one tile and share every W stage, so each
+// MMA needs 1.5x fewer operand bytes from L2 (32 KB per 128 x 256 x 32 product
+// instead of 48 KB); chosen where it also leaves fewer rounds of tiles.
+template <int BN, int MB = 1>
 struct TCfg {
     static_assert(BN == 128 || BN == 256, "cta_group::1 MMA with M 128 takes N % 16 == 0, N <= 256");
-    static constexpr uint32_t kTileB = BN * kTBK * 4;  // W rows per stage
+    static_assert(MB == 1 || (MB == 2 && BN == 256), "two row halves use the 512 tensor-memory columns");
+    static constexpr uint32_t kTileA = MB * kTBM * kTBK * 4;  // X rows per stage (16 KB per half)
+    static constexpr uint32_t kTileB = BN * kTBK * 4;         // W rows per stage
     static constexpr uint32_t kStageBytes = kTileA + kTileB;
-    static constexpr int kStages = BN == 256 ? 4 : 6;  // 192 KB of ring either way: one CTA per SM
+    static constexpr int kStages = MB == 2 ? 3 : BN == 256 ? 4 : 6;  // 192 KB of ring: one CTA per SM
     static constexpr uint32_t kAccCols = BN;            // one F32 accumulator: 128 lanes x BN columns
-    static constexpr uint32_t kTmemCols = 2 * BN;       // two, so a tile's epilogue overlaps the next tile's MMAs
+    static constexpr uint32_t kTmemCols = 2 * BN;       // two accumulators
     static constexpr size_t kSmem = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes + 256;
     // kind::tf32, both operands K-major
     static constexpr uint32_t kIdesc = idesc_tf32(kTBM, BN, false, false);
@@ -68,22 +74,23 @@ __device__ int32_t g_tf32_status;  // status word when the caller passes none
 struct TileIx {
     int64_t m0, n0, kbeg, kend;
 };
-template <int BN>
+template <int BN, int MB>
 B200_DEVICE TileIx tile_of(const GemmArgs &a, int64_t t, int64_t mt, int64_t nt) {
     const int64_t z = t / (mt * nt), r = t % (mt * nt);
     TileIx ix;
-    ix.m0 = (r % mt) * kTBM;
+    ix.m0 = (r % mt) * kTBM * MB;
     ix.n0 = (r / mt) * BN;
     ix.kbeg = a.k_split ? z * a.k_split : 0;
     ix.kend = a.k_split ? min64(a.K, ix.kbeg + a.k_split) : a.K;
     return ix;
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, int MB>
 __global__ void __launch_bounds__(kTThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const GemmArgs a,
                      int64_t n_tiles) {
-    using C = TCfg<BN>;
+    using C = TCfg<BN, MB>;
+    constexpr uint32_t kTileA = C::kTileA;
     constexpr int kTStages = C::kStages;
     constexpr uint32_t kStageBytes = C::kStageBytes, kAccCols = C::kAccCols, kTmemCols = C::kTmemCols;
     extern __shared__ unsigned char smem_raw[];
@@ -98,7 +105,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     int32_t *status = a.status ? a.status : &g_tf32_status;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t mt = (a.M + kTBM - 1) / kTBM, nt = (a.N + BN - 1) / BN;
+    const int64_t mt = (a.M + kTBM * MB - 1) / (kTBM * MB), nt = (a.N + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
@@ -134,7 +141,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             bool ok = true;
 #pragma unroll 1
             for (int64_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                const TileIx ix = tile_of<BN>(a, t, mt, nt);
+                const TileIx ix = tile_of<BN, MB>(a, t, mt, nt);
 #pragma unroll 1
                 for (int64_t k = ix.kbeg; k < ix.kend; k += kTBK, ++it) {
                     const int s = it % kTStages;
@@ -161,9 +168,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
             bool ok = true;
 #pragma unroll 1
             for (int64_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++j) {
-                const TileIx ix = tile_of<BN>(a, t, mt, nt);
-                const int b = j & 1;
-                if (j >= 2 && !wait_bounded(&acc_free[b], ((j >> 1) - 1) & 1, status)) break;
+                const TileIx ix = tile_of<BN, MB>(a, t, mt, nt);
+                // MB = 1: accumulator b = j % 2, free again once tile j - 2 is read out;
+                // MB = 2: both accumulators for tile j, free once tile j - 1 is read out
+                const int b = MB == 2 ? 0 : (j & 1);
+                if (MB == 1 && j >= 2 && !wait_bounded(&acc_free[b], ((j >> 1) - 1) & 1, status)) break;
+                if (MB == 2 && j >= 1 && !wait_bounded(&acc_free[0], (j - 1) & 1, status)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + b * kAccCols;
                 bool first = true;
@@ -179,7 +189,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     const uint64_t db = desc_k_sw128(sbase + s * kStageBytes + kTileA);
 #pragma unroll
                     for (int kk = 0; kk < kTBK / 8; ++kk) {  // K 8 per MMA: +32 bytes = +2 in the address field
-                        tc_mma_tf32(acc, da + 2 * kk, db + 2 * kk, C::kIdesc, first ? 0u : 1u);
+#pragma unroll
+                        for (int half = 0; half < MB; ++half)  // X rows 128 half.. (16 KB further), accumulator half
+                            tc_mma_tf32(acc + half * kAccCols, da + half * (16384 >> 4) + 2 * kk, db + 2 * kk,
+                                        C::kIdesc, first ? 0u : 1u);
                         first = false;
                     }
                     tc_commit(smem_addr(&empty[s]));
@@ -188,7 +201,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
             }
             // no MMA may still write tensor memory when it is freed (matters only if
             // the epilogue gave up early)
-            if (j > 0) wait_bounded(&acc_full[(j - 1) & 1], ((j - 1) >> 1) & 1, nullptr);
+            if (j > 0) {
+                if (MB == 2)
+                    wait_bounded(&acc_full[0], (j - 1) & 1, nullptr);
+                else
+                    wait_bounded(&acc_full[(j - 1) & 1], ((j - 1) >> 1) & 1, nullptr);
+            }
         }
     } else {
         // ---- epilogue warps: thread (warp w, lane t) owns tile row 32 * (w % 4) + t
@@ -199,14 +217,16 @@ __global__ void __launch_bounds__(kTThreads, 1)
         int j = 0;
 #pragma unroll 1
         for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++j) {
-            const TileIx ix = tile_of<BN>(a, t, mt, nt);
-            const int b = j & 1;
+            const TileIx ix = tile_of<BN, MB>(a, t, mt, nt);
+            const int b = MB == 2 ? 0 : (j & 1);
             // warp-uniform: tcgen05.ld is a warp-collective (.sync.aligned) instruction
-            if (!__all_sync(0xffffffffu, wait_bounded(&acc_full[b], (j >> 1) & 1, status))) break;
+            if (!__all_sync(0xffffffffu, wait_bounded(&acc_full[b], MB == 2 ? (j & 1) : ((j >> 1) & 1), status))) break;
             tc_fence_after();
-            const int64_t gm = ix.m0 + 32 * q + lane;
-            const uint32_t trow = tmem + b * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
             const int64_t z = t / (mt * nt);
+#pragma unroll 1
+            for (int half = 0; half < MB; ++half) {  // row half of the tile: accumulator b + half
+            const int64_t gm = ix.m0 + kTBM * half + 32 * q + lane;
+            const uint32_t trow = tmem + (b + half) * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
@@ -264,9 +284,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                 }
             }
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_free[b]);  // the MMA warp may reuse accumulator b
+            if (lane == 0) mbar_arrive(&acc_free[b]);  // the MMA warp may reuse accumulator b (MB = 2: both)
         }
     }
     tc_fence_before();
@@ -285,18 +306,34 @@ bool encode(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int
     return tma_encode_f32(map, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, int MB = 1>
 cudaError_t launch_epi(const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a, int64_t n_tiles,
                        cudaStream_t st, bool pdl) {
+    auto kern = gemm_tf32_kernel<EPI, BN, MB>;
     {
-        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(gemm_tf32_kernel<EPI, BN>), ATTR_SMEM, [] {
-            return cudaFuncSetAttribute(gemm_tf32_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(TCfg<BN>::kSmem));
+        const cudaError_t e = once_per_device(reinterpret_cast<const void *>(kern), ATTR_SMEM, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(TCfg<BN, MB>::kSmem));
         });
         if (e != cudaSuccess) return e;
     }
     const dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_tiles, device_sm_count())));
-    return b200_launch(gemm_tf32_kernel<EPI, BN>, grid, dim3(kTThreads), TCfg<BN>::kSmem, st, pdl, mx, mw, a, n_tiles);
+    return b200_launch(kern, grid, dim3(kTThreads), TCfg<BN, MB>::kSmem, st, pdl, mx, mw, a, n_tiles);
+}
+
+// 256 x 256 tiles, no K split.
+cudaError_t launch_m2(const GemmArgs &a_in, cudaStream_t stream, bool pdl) {
+    GemmArgs a = a_in;
+    a.k_split = 0;
+    CUtensorMap mx, mw;
+    if (!encode(&mx, a.x, a.M, a.K, a.ldx, 2 * kTBM) || !encode(&mw, a.w, a.N, a.K, a.K, 256)) return cudaErrorNotSupported;
+    const int64_t n_tiles = ((a.N + 255) / 256) * ((a.M + 2 * kTBM - 1) / (2 * kTBM));
+    switch (a.epi) {
+        case GEMM_STORE: return launch_epi<GEMM_STORE, 256, 2>(mx, mw, a, n_tiles, stream, pdl);
+        case GEMM_RESIDUAL: return launch_epi<GEMM_RESIDUAL, 256, 2>(mx, mw, a, n_tiles, stream, pdl);
+        case GEMM_SWIGLU: return launch_epi<GEMM_SWIGLU, 256, 2>(mx, mw, a, n_tiles, stream, pdl);
+    }
+    return cudaErrorInvalidValue;
 }
 
 // K splits of the tcgen05 GEMM with BN-wide tiles, when the tile grid alone leaves
@@ -359,9 +396,19 @@ cudaError_t gemm_tf32_launch(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     if ((a.K & 3) || (a.ldx & 3) || (reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
         a.M >= (int64_t(1) << 31) || a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 31))
         return cudaErrorNotSupported;
-    // 256-wide tiles (half the X traffic per flop) once they alone fill the SMs
+    // 256-wide tiles (half the X traffic per flop) once they alone fill the SMs; 256 x 256
+    // tiles where they need at most half the rounds of 128 x 256 ones (measured: a
+    // 256 x 256 tile takes ~1.9x a 128 x 256 one, so they win only on equal work per
+    // SM, by their lower operand traffic: 4096^3 605 -> 699 TFLOP/s, 2048 x 4096 x 1024
+    // 399 -> 420; with more rounds, e.g. 2048 x 6144 x 1024, they lose)
+    const int64_t sms = device_sm_count();
     const int64_t tiles256 = ((a.N + 255) / 256) * ((a.M + kTBM - 1) / kTBM);
-    return tiles256 >= device_sm_count() ? launch_bn<256>(a, stream, pdl) : launch_bn<128>(a, stream, pdl);
+    const int64_t tiles2 = ((a.N + 255) / 256) * ((a.M + 2 * kTBM - 1) / (2 * kTBM));
+    if (a.M > kTBM && 2 * tiles2 >= sms && 2 * ((tiles2 + sms - 1) / sms) <= (tiles256 + sms - 1) / sms) {
+        const cudaError_t e = launch_m2(a, stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    return tiles256 >= sms ? launch_bn<256>(a, stream, pdl) : launch_bn<128>(a, stream, pdl);
 }
 
 }  // namespace b200

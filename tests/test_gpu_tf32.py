@@ -53,6 +53,8 @@ SHAPES = [  # (M, N, K): prompt rows x output features x inner size
     (130, 264, 1056),    # ragged N and M, K not a multiple of 128
     (5, 8, 64),          # one tile, mostly padding
     (257, 136, 1028),    # K % 32 == 4: zero-filled K tail
+    (2048, 4096, 1024),  # QKV of a 2048-token prompt: 256 x 256 tiles (two row halves per tile)
+    (1000, 9000, 520),   # 256 x 256 tiles with ragged M, N and K
 ]
 
 
