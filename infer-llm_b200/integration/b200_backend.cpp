@@ -104,6 +104,14 @@ size_t env_mb(const char *name, size_t def_mb) {
     return static_cast<size_t>(x > 0 ? x : 0) << 20;
 }
 
+// Prefill precision of the engine steps: B200_PREFILL_PRECISION=tf32 selects the
+// tcgen05 TF32 prefill (GEMMs and attention, the stated 2e-3 logit bound); anything
+// else, or unset, the exact F32 path. Decode is exact either way.
+int32_t prefill_precision() {
+    const char *v = std::getenv("B200_PREFILL_PRECISION");
+    return (v && std::strcmp(v, "tf32") == 0) ? B200_PREC_TF32 : B200_PREC_FFMA;
+}
+
 bool named(const Tensor *t, const std::string &n) { return t && t->name == n; }
 
 // The host tensor behind a scheduler copy ("<name>_##copy##", src[0] = the source).
@@ -408,7 +416,7 @@ private:
         c.rms_eps = s.eps;
         c.tied = 0;          // the reference keeps a device copy named output.weight
         c.kv_capacity = static_cast<int32_t>(cap);
-        c.precision = B200_PREC_FFMA;
+        c.precision = prefill_precision();
         c.tp_world = 1;
         c.external_kv = 1;
         c.max_batch = static_cast<int32_t>(std::max<int64_t>(s.M, 512));

@@ -80,3 +80,35 @@ def test_reference_engine_on_b200_backend_06b_tokens(ref_be, ref):
     print(f"reference Runner decode: CPU backend {rate[0]:.1f} tok/s, B200 Backend {rate[1]:.1f} tok/s")
     agree = float(np.mean(np.array(runs[0]) == np.array(runs[1])))
     assert agree >= 0.99, runs
+
+
+def test_reference_engine_on_b200_backend_06b_tf32_prefill(ref_be, ref, monkeypatch):
+    """B200_PREFILL_PRECISION=tf32: the Backend's engine prefills on the tcgen05 TF32
+    path (GEMMs and attention). Qwen3-0.6B shape, 32-token prompt: the prefill logits
+    within the stated TF32 bound (2e-3 of the largest logit) of the reference CPU
+    engine's, and the same greedy tokens over 8 teacher-forced decode steps (decode
+    stays exact)."""
+    cfg = G.QWEN3_0_6B
+    path = G.cached_model(cfg, 0)
+    prompt = np.random.default_rng(5).integers(0, cfg.n_vocab, 32).astype(np.int32)
+    monkeypatch.setenv("B200_PREFILL_PRECISION", "tf32")
+    runs = []
+    for lib, dev in ((ref, None), (ref_be, 0)):
+        eng = oracle.RefEngine(lib, path, threads=THREADS, capacity=64, cuda_device=dev)
+        try:
+            lg = np.empty(cfg.n_vocab, np.float32)
+            toks = [eng.eval(prompt, lg)]
+            first = lg.copy()
+            for i in range(8):  # teacher-forced with the CPU engine's tokens
+                nxt = runs[0][0][i] if runs else toks[-1]
+                toks.append(eng.eval(np.array([nxt], np.int32), lg))
+            if dev is not None:
+                assert eng.backend_counters() == (9, 0)
+            runs.append((toks, first))
+        finally:
+            eng.close()
+    (cpu_toks, cpu_lg), (gpu_toks, gpu_lg) = runs
+    err = float(np.max(np.abs(gpu_lg - cpu_lg)) / np.max(np.abs(cpu_lg)))
+    print(f"Backend TF32 prefill: max |dlogit| / max |logit| = {err:.3g}")
+    assert err <= 2e-3
+    assert gpu_toks == cpu_toks
