@@ -89,10 +89,10 @@ B200_DEVICE float fast_exp2(float x) {
     return y;
 }
 
-// Rounds the N16 16-byte groups at p to TF32; thread i of kCvtThreads takes groups
-// i, i + kCvtThreads, ... (eight loads in flight). In a K / V tile (8 KB boxes of 64
-// rows of 128 bytes) the groups of rows >= valid_rows are cleared instead; Q and
-// whole K / V tiles pass valid_rows = 64.
+// Rounds the N16 16-byte groups of a K / V tile at p (8 KB boxes of 64 rows of 128
+// bytes) to TF32; thread i of kCvtThreads takes groups i, i + kCvtThreads, ... (eight
+// loads in flight); the groups of rows >= valid_rows are cleared instead (a whole
+// tile passes valid_rows = 64).
 template <int N16>
 B200_DEVICE void round_tf32_smem(unsigned char *p, int valid_rows, int i) {
     static_assert(N16 % (8 * kCvtThreads) == 0, "whole rounds of eight groups per thread");
@@ -129,8 +129,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *v_empty = bars + 12;  // [3]
     uint64_t *v_ready = bars + 15;  // [3] V stage rounded (rows past the sequence cleared)
     uint64_t *s_full = bars + 18;   // [2] S buffer complete (and every earlier product)
-    uint64_t *p_full = bars + 20;   // [2] P written over S (and O rescaled), 128 arrivals
-    uint64_t *q_ready = bars + 22;  // Q in tensor memory, 128 arrivals
+    uint64_t *p_full = bars + 20;   // [2] P written over S (and O rescaled), one arrival per softmax thread
+    uint64_t *q_ready = bars + 22;  // Q in tensor memory, one arrival per softmax thread
     uint64_t *o_done = bars + 23;   // one phase per tile: P_t V_t complete
     uint64_t *o_final = bars + 24;  // the last P V complete
     uint64_t *mma_idle = bars + 25; // no tensor-core work in flight (exit)
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 0 || warp == kVWarp) {
         if (lane == 0) {
-            // ---- TMA engine: K (warp 0) or V (warp 10), stage t % 3
+            // ---- TMA engine: K (warp 0) or V (warp kVWarp), stage t % 3
             const bool is_k = warp == 0;
             const CUtensorMap *map = is_k ? &tk : &tv;
             uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
