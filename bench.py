@@ -407,6 +407,8 @@ def run_b200(args):
         res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_threads, sample_steps=args.cpu_sample_steps)
     res["first_tokens"] = [int(first)] + [int(t) for t in toks[:8]]
     eng.close()
+    if rank == 0 and world == 1 and args.model == "0.6b" and not args.no_prefill_ops:
+        res["prefill_ops"] = prefill_ops_block()
     if args.model == "0.6b" and not args.no_tp_8b:
         # the model that shards: Qwen3-8B tensor-parallel over the same N GPUs (TP1 at N = 1)
         res["tp_8b"] = tp_8b_block(world, rank, local, steps, warm)
@@ -414,6 +416,35 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank == 0:
         emit(res)
+
+
+def prefill_ops_block():
+    """The prefill kernels at BASELINE configs[1]-[2] shapes, timed through the C ABI
+    after the decode measurement (same op timer as --op: CUDA events on the launching
+    stream, L2 flushed between launches, median of 20): one layer's causal attention at
+    S = 2048 on the exact FFMA path and on the tcgen05 TF32 path, the TF32 GEMM on
+    2048 x 4096 x 1024 (the QKV product of a 2048-token prompt), and the exact FFMA GEMM
+    on the five layer shapes at M = 256 (prompt-sized, split K in one wave). FFMA
+    fractions are of 148 SMs x 128 lanes x 2 flop x 1.965 GHz; the TF32 one of half the
+    measured bf16 burst peak."""
+    ffma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    tf32_peak = None
+    try:
+        tf32_peak = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))).get("bf16_tflops") / 2
+    except Exception:
+        pass
+    out = {}
+    for prec, name in ((0, "attn_s2048_ffma"), (1, "attn_s2048_tf32")):
+        r = op_case(dict(op="attn", K=0, N=0, M=2048, L=2048, precision=prec), 20, 5)
+        out[name] = {"us": r["us_median"], "tflops": r["tflops"]}
+    r = op_case(dict(op="gemm", K=1024, N=4096, M=2048, L=0, precision=1), 20, 5)
+    out["gemm_tf32_2048x4096x1024"] = {"us": r["us_median"], "tflops": r["tflops"],
+                                       "frac": round(r["tflops"] / tf32_peak, 4) if tf32_peak else None}
+    for K, N in [(1024, 2048), (1024, 1024), (2048, 1024), (1024, 3072), (3072, 1024)]:
+        r = op_case(dict(op="gemm", K=K, N=N, M=256, L=0, precision=0), 20, 5)
+        out[f"gemm_ffma_256x{N}x{K}"] = {"us": r["us_median"], "tflops": r["tflops"],
+                                         "frac": round(r["tflops"] / ffma_peak, 4)}
+    return out
 
 
 def tp_8b_block(world, rank, local, steps, warm, plen=PROMPT_LEN):
@@ -694,6 +725,8 @@ def main():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--cpu-sample-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill-ops", action="store_true",
+                    help="leave out the prefill_ops block (one-layer attention and GEMM timings)")
     ap.add_argument("--no-tp-8b", action="store_true",
                     help="skip the Qwen3-8B tensor-parallel block of the default (0.6B) run")
     ap.add_argument("--decode", choices=["auto", "multi", "single"], default="auto",

@@ -1,7 +1,7 @@
 // 5th-generation tensor-core (tcgen05) building blocks shared by the sm_100a
 // kernels: shared-memory matrix descriptors, kind::tf32 MMAs with the A operand in
-// shared or tensor memory, commits, tensor-memory loads / stores, and a bounded
-// mbarrier wait.
+// shared or tensor memory, commits, tensor-memory loads / stores, and bounded
+// mbarrier waits.
 #pragma once
 
 #include "common.cuh"
