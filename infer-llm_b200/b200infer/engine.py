@@ -34,11 +34,14 @@ class Engine:
 
     def __init__(self, cfg: Qwen3Config, kv_capacity: int, max_batch: int = 512, device: int = 0,
                  precision: int = PREC_FFMA, tp_rank: int = 0, tp_world: int = 1,
-                 decode_mode: int = DECODE_AUTO):
+                 decode_mode: int = DECODE_AUTO, external_kv: bool = False):
+        """external_kv: the K/V cache of every layer is caller memory, bound with
+        bind_kv before finalize (as the Backend drop-in binds the reference's KV
+        objects)."""
         self.cfg = cfg
         self._c = _Cfg(cfg.n_vocab, cfg.n_embd, cfg.n_layer, cfg.n_head, cfg.n_head_kv, cfg.head_dim,
                        cfg.n_ff, cfg.n_ctx_train, cfg.rope_theta, cfg.rms_eps, int(cfg.tied),
-                       kv_capacity, max_batch, precision, tp_rank, tp_world, decode_mode, 0)
+                       kv_capacity, max_batch, precision, tp_rank, tp_world, decode_mode, int(external_kv))
         h = C.c_void_p()
         _chk("b200_engine_create", lib().b200_engine_create(C.byref(self._c), device, C.byref(h)))
         self.h = h
@@ -64,6 +67,12 @@ class Engine:
         arr = np.ascontiguousarray(arr, np.float32)
         _chk("b200_engine_set_weight " + name,
              lib().b200_engine_set_weight(self.h, name.encode(), C.c_void_p(arr.ctypes.data), arr.size))
+
+    def bind_kv(self, layer: int, k, v):
+        """Layer `layer`'s K and V cache: device tensors of kv_capacity x n_head_kv x
+        head_dim floats (token-major), kept alive by the caller."""
+        _chk("b200_engine_bind_kv", lib().b200_engine_bind_kv(self.h, layer, C.c_void_p(k.data_ptr()),
+                                                              C.c_void_p(v.data_ptr())))
 
     def load_gguf(self, path: str, staging_bytes: int = 0):
         """All tensors of a GGUF file through the native loader (memory-mapped,

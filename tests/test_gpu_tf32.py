@@ -196,3 +196,45 @@ def test_tf32_qwen3_06b_prefill(cuda, port, plen):
         agree.append(tok == ref)
     assert all(agree), agree
     eng.close()
+
+
+@pytest.mark.parametrize("decode", [B.DECODE_AUTO, B.DECODE_MULTI], ids=["single_launch", "multi_kernel"])
+@pytest.mark.parametrize("precision", [B.PREC_TF32, B.PREC_FFMA], ids=["tf32", "ffma"])
+def test_prefill_ignores_cache_rows_past_the_sequence(cuda, precision, decode):
+    """Engine prefill over caller-bound K/V caches (external_kv, as the Backend
+    drop-in binds the reference's KV objects) whose rows past the sequence hold NaN.
+    TF32: the tensor-core attention's tensor maps cover the whole capacity, so the
+    last key tile (a 40-token prompt: keys 40..63 of the first 64-key tile) reads
+    them; their scores are masked and their V rows cleared in shared memory. FFMA:
+    the tiled kernel never loads them. Then three decode steps (positions 40..42) on
+    the single-launch or the multi-kernel path, whose attention tiles reach past the
+    sequence as well. Every logit vector is finite and bit-identical to a run over
+    zero-filled caches."""
+    cfg = G.QWEN3_0_6B
+    cap = 96
+    prompt = np.random.default_rng(11).integers(0, cfg.n_vocab, 40).astype(np.int32)
+    out = []
+    for fill in (0.0, float("nan")):
+        eng = B.Engine(cfg, kv_capacity=cap, max_batch=64, precision=precision, external_kv=True,
+                       decode_mode=decode)
+        shape = (cap, cfg.n_head_kv, cfg.head_dim)
+        caches = [(torch.full(shape, fill, device=cuda), torch.full(shape, fill, device=cuda))
+                  for _ in range(cfg.n_layer)]
+        for l, (k, v) in enumerate(caches):
+            eng.bind_kv(l, k, v)
+        eng.init_random(21).finalize()
+        lg = np.empty(cfg.n_vocab, np.float32)
+        toks, lgs = [eng.eval(prompt, lg)], [lg.copy()]
+        torch.cuda.synchronize()
+        # rows past the prompt are as they were
+        assert bool(torch.isnan(caches[0][0][40:]).all()) == (fill != fill)
+        for t in (5, 6, 7):
+            toks.append(eng.eval(np.array([t], np.int32), lg))
+            lgs.append(lg.copy())
+        out.append((toks, lgs))
+        eng.close()
+        del caches
+    assert out[0][0] == out[1][0]
+    for a, b in zip(out[0][1], out[1][1]):
+        assert np.all(np.isfinite(b))
+        assert np.array_equal(a, b)
