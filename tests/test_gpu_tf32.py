@@ -238,3 +238,28 @@ def test_prefill_ignores_cache_rows_past_the_sequence(cuda, precision, decode):
     for a, b in zip(out[0][1], out[1][1]):
         assert np.all(np.isfinite(b))
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("precision", [B.PREC_TF32, B.PREC_FFMA], ids=["tf32", "ffma"])
+def test_flash_attn_strided_cache_views(cuda, precision):
+    """K / V as views into a wider cache (token stride (Hkv + 2) * D, head stride D,
+    as a cache that interleaves other rows between tokens would give): the prefill
+    kernels read through the caller's strides (the tensor-core kernel builds its TMA
+    maps from them), so the result is bit-identical to the same rows passed
+    contiguously, on both precisions."""
+    Tq, n_past, Hq, Hkv, D = 300, 40, 16, 8, 128
+    L = n_past + Tq
+    g = torch.Generator(device=cuda).manual_seed(17)
+    q = torch.randn((Tq, Hq, D), device=cuda, generator=g)
+    kbuf = torch.randn((L, Hkv + 2, D), device=cuda, generator=g)
+    vbuf = torch.randn((L, Hkv + 2, D), device=cuda, generator=g)
+    k, v = kbuf[:, 1:Hkv + 1, :], vbuf[:, 1:Hkv + 1, :]  # offset one head: base 512 B in
+    want = B.flash_attn(q, k.contiguous(), v.contiguous(), n_past, precision=precision)
+    out = torch.empty_like(q)
+    tok = (Hkv + 2) * D
+    rc = B.lib().b200_flash_attn_ex(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), D, Hq, Hkv, Tq, L, n_past, 0.0,
+        tok, D, tok, D, None, 0, None, precision)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
